@@ -1,0 +1,163 @@
+// Shared helpers of the aps2026_b200 kernels: status reporting, 128-bit
+// global memory access, block reductions and launch geometry for sm_100a.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/aps2026_b200.h"
+
+namespace b2 {
+
+// ---- host-side status -------------------------------------------------------
+
+// Records the calling thread's last failure message; returns `code`.
+int set_error(int code, const std::string& message);
+
+inline int invalid(const std::string& message) {
+    return set_error(B2_ERR_INVALID_ARGUMENT, message);
+}
+
+// Converts the launch status of the kernels just enqueued into a b2 status.
+inline int launch_result(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return set_error(B2_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    return B2_OK;
+}
+
+inline cudaStream_t as_stream(b2_stream_t s) { return static_cast<cudaStream_t>(s); }
+
+__host__ __device__ inline bool aligned16(const void* p) {
+    return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0;
+}
+
+// Number of SMs of the current device (148 on B200), cached per device.
+int sm_count();
+
+// Resident CTAs per SM for `kernel` at `threads` threads and `smem` bytes of
+// dynamic shared memory on the current device.
+int resident_ctas(const void* kernel, int threads, std::size_t smem);
+
+// Grid for a grid-stride loop over `units`: at most the number of CTAs that
+// are resident at once (one full wave), at least 1.
+inline unsigned wave_grid(const void* kernel, int threads, std::size_t smem,
+                          std::size_t units) {
+    const std::size_t wave =
+        static_cast<std::size_t>(sm_count()) * static_cast<std::size_t>(resident_ctas(kernel, threads, smem));
+    std::size_t g = units < wave ? units : wave;
+    if (g == 0) g = 1;
+    return static_cast<unsigned>(g);
+}
+
+// ---- in-kernel bounds checks -------------------------------------------------
+//
+// Every kernel that dereferences a caller-provided index checks it, skips
+// the access when it is out of range, and ORs a B2_CHECK_* bit into this
+// per-translation-unit word, which b2_device_status() collects and clears.
+// No kernel traps or asserts.
+static __device__ unsigned int g_check_word;
+
+__device__ __forceinline__ void flag_check(unsigned int bit) {
+    atomicOr(&g_check_word, bit);
+}
+
+// Host side of the per-TU word: adds its value to *acc and clears it.
+inline int take_check_word(cudaStream_t stream, unsigned int* acc) {
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_check_word, sizeof(v), 0,
+                                              cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess && v != 0) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbolAsync(g_check_word, &zero, sizeof(zero), 0,
+                                    cudaMemcpyHostToDevice, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    }
+    if (e != cudaSuccess)
+        return set_error(B2_ERR_CUDA, std::string("b2_device_status: ") + cudaGetErrorString(e));
+    *acc |= v;
+    return B2_OK;
+}
+
+// ---- 128-bit global access ----------------------------------------------------
+
+// Streaming read of data this kernel reads once (read-only path, no L1
+// allocation).
+__device__ __forceinline__ float4 ld_stream(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Plain coherent read, for operands the same kernel also writes (in-place
+// x of add-LN, q/k of RoPE), which must not take the read-only path.
+__device__ __forceinline__ float4 ld_plain(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_plain(float4* p, const float4& v) {
+    asm volatile("st.global.v4.f32 [%0], {%1,%2,%3,%4};"
+                 :
+                 : "l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+// ---- reductions ------------------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide sum of one value per thread, returned to every thread.
+// `scratch` holds at least WARPS floats; consecutive calls must alternate
+// scratch buffers (or be separated by a barrier) so a fast warp cannot
+// overwrite a slot a slow warp is still reading.
+template <int WARPS>
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+    v = warp_sum(v);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float t = lane < WARPS ? scratch[lane] : 0.0f;
+    return warp_sum(t);
+}
+
+template <int WARPS>
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+    v = warp_max(v);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float t = lane < WARPS ? scratch[lane] : -3.402823466e+38F;
+    return warp_max(t);
+}
+
+}  // namespace b2
+
+// Per-TU status collector registration: each .cu that has kernels with bounds
+// checks defines one of these, and b2_device_status calls them all.
+#define B2_DEFINE_CHECK_TAKER(name)                                              \
+    namespace b2 {                                                               \
+    int take_check_##name(cudaStream_t stream, unsigned int* acc) {              \
+        return take_check_word(stream, acc);                                     \
+    }                                                                            \
+    }

@@ -1,0 +1,454 @@
+// MoE routing (top-2 selection + stable token->expert permutation), gated
+// SiLU, weighted un-permute, and the plain residual add.
+//
+// Routing reference (src/tensor.cu): k_moe_top2 (:1293-1331) picks experts
+// and bumps 16 global atomics per token pair; k_moe_offsets_work
+// (:1337-1374) scans the counts on ONE thread and fills the work queues;
+// k_moe_fill_stable (:1376-1418) runs 16 CTAs, each scanning ALL T tokens
+// for its expert -- 16x the routes traffic on 16 of 148 SMs.
+//
+// Here the same outputs come from two launches over 256-token tiles:
+//   1. route_select: per token the quantized scores and the scan-order
+//      top-2 pick (same float operations and comparisons as k_moe_top2),
+//      per tile an expert histogram in shared memory. The last tile to
+//      finish (an atomic ticket, no waiting) scans the per-tile histograms
+//      for every expert (warp-parallel), writes counts / offsets and both
+//      work queues, and re-arms the ticket.
+//   2. route_scatter: per tile, warp ballots give each token's stable rank
+//      among the tile's tokens of the same expert; rank + tile prefix +
+//      expert offset is the position, written to assignment_rows and
+//      route_positions. Token order within an expert is ascending, which is
+//      exactly what k_moe_fill_stable produces.
+// The integer outputs are bit-identical to the reference's.
+#include "rowload.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int kTile = 256;          // tokens per routing tile = threads per CTA
+constexpr int kMaxExperts = 32;
+constexpr std::size_t kWsHeader = 256;  // ticket word + padding
+
+struct RouteArgs {
+    const float* logits;
+    std::size_t T, E;
+    float quantum, tie_eps;
+    std::uint8_t* routes;
+    std::uint32_t* counts;
+    std::uint32_t* offsets;
+    std::uint32_t* assignment_rows;
+    std::uint32_t* route_positions;
+    std::uint32_t* we64;
+    std::uint32_t* ws64;
+    std::uint32_t* we128;
+    std::uint32_t* ws128;
+    std::uint32_t* ticket;       // workspace word 0
+    std::uint32_t* tile_counts;  // [tiles][E], becomes per-expert exclusive prefix
+    std::size_t tiles;
+};
+
+// sign(s) * floorf(|s| / quantum + 0.5f) * quantum, the reference's
+// canonicalisation (src/tensor.cu:1301-1305), with every operation rounded
+// separately (no contraction is possible in the reference expression).
+__device__ __forceinline__ float quantize(float s, float quantum) {
+    const float r = __fmul_rn(floorf(__fadd_rn(__fdiv_rn(fabsf(s), quantum), 0.5f)), quantum);
+    return s < 0.0f ? -r : r;
+}
+
+__global__ void __launch_bounds__(kTile)
+route_select(RouteArgs a) {
+    __shared__ unsigned int hist[kMaxExperts];
+    __shared__ unsigned int totals[kMaxExperts];
+    __shared__ unsigned int offs[kMaxExperts + 1], q64[kMaxExperts + 1], q128[kMaxExperts + 1];
+    __shared__ bool is_last;
+    const unsigned E = static_cast<unsigned>(a.E);
+    if (threadIdx.x < E) hist[threadIdx.x] = 0;
+    __syncthreads();
+
+    const std::size_t t = static_cast<std::size_t>(blockIdx.x) * kTile + threadIdx.x;
+    if (t < a.T) {
+        float sc[kMaxExperts];
+        const float* row = a.logits + t * a.E;
+        if ((E & 3u) == 0 && aligned16(row)) {
+#pragma unroll
+            for (unsigned e = 0; e < kMaxExperts; e += 4)
+                if (e < E) {
+                    const float4 v = ld_stream(reinterpret_cast<const float4*>(row + e));
+                    sc[e] = v.x; sc[e + 1] = v.y; sc[e + 2] = v.z; sc[e + 3] = v.w;
+                }
+        } else {
+#pragma unroll
+            for (unsigned e = 0; e < kMaxExperts; ++e)
+                if (e < E) sc[e] = __ldg(row + e);
+        }
+        int first = -1;
+        float first_value = -3.402823466e+38F;
+#pragma unroll
+        for (unsigned e = 0; e < kMaxExperts; ++e)
+            if (e < E) {
+                sc[e] = quantize(sc[e], a.quantum);
+                if (first < 0 || sc[e] > __fadd_rn(first_value, a.tie_eps)) {
+                    first = static_cast<int>(e);
+                    first_value = sc[e];
+                }
+            }
+        int second = -1;
+        float second_value = -3.402823466e+38F;
+#pragma unroll
+        for (unsigned e = 0; e < kMaxExperts; ++e)
+            if (e < E && static_cast<int>(e) != first) {
+                if (second < 0 || sc[e] > __fadd_rn(second_value, a.tie_eps)) {
+                    second = static_cast<int>(e);
+                    second_value = sc[e];
+                }
+            }
+        const unsigned short pair =
+            static_cast<unsigned short>(first) | (static_cast<unsigned short>(second) << 8);
+        reinterpret_cast<unsigned short*>(a.routes)[t] = pair;
+        atomicAdd(&hist[first], 1u);
+        atomicAdd(&hist[second], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < E) a.tile_counts[static_cast<std::size_t>(blockIdx.x) * E + threadIdx.x] = hist[threadIdx.x];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!is_last) return;
+
+    // ---- last tile: per-expert scan over tiles, counts, offsets, queues ----
+    __threadfence();
+    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (unsigned e = warp; e < E; e += kTile / 32) {
+        unsigned running = 0;
+        for (std::size_t base = 0; base < a.tiles; base += 32) {
+            const std::size_t tile = base + lane;
+            const unsigned c = tile < a.tiles ? __ldcg(a.tile_counts + tile * E + e) : 0u;
+            unsigned incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= static_cast<unsigned>(o)) incl += n;
+            }
+            if (tile < a.tiles) a.tile_counts[tile * E + e] = running + incl - c;
+            running += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) totals[e] = running;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned off = 0, w64 = 0, w128 = 0;
+        for (unsigned e = 0; e < E; ++e) {
+            a.counts[e] = totals[e];
+            a.offsets[e] = off;
+            offs[e] = off;
+            q64[e] = w64;
+            q128[e] = w128;
+            off += totals[e];
+            w64 += (totals[e] + 63) / 64;
+            w128 += (totals[e] + 127) / 128;
+        }
+        a.offsets[E] = off;
+        q64[E] = w64;
+        q128[E] = w128;
+        *a.ticket = 0;  // re-armed for the next call
+    }
+    __syncthreads();
+    const std::size_t n64 = (2 * a.T + 63) / 64 + a.E, n128 = (2 * a.T + 127) / 128 + a.E;
+    // Queue entry i belongs to the expert whose chunk range holds it; entries
+    // past the last chunk are 0xFFFFFFFF (the reference memsets the expert
+    // queues to 0xff; the start queues get the same marker here).
+    for (std::size_t i = threadIdx.x; i < n64; i += kTile) {
+        std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
+        if (i < q64[E]) {
+            unsigned e = 0;
+            while (i >= q64[e + 1]) ++e;
+            ex = e;
+            st = offs[e] + static_cast<std::uint32_t>(i - q64[e]) * 64u;
+        }
+        if (a.we64) a.we64[i] = ex;
+        if (a.ws64) a.ws64[i] = st;
+    }
+    for (std::size_t i = threadIdx.x; i < n128; i += kTile) {
+        std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
+        if (i < q128[E]) {
+            unsigned e = 0;
+            while (i >= q128[e + 1]) ++e;
+            ex = e;
+            st = offs[e] + static_cast<std::uint32_t>(i - q128[e]) * 128u;
+        }
+        if (a.we128) a.we128[i] = ex;
+        if (a.ws128) a.ws128[i] = st;
+    }
+}
+
+__global__ void __launch_bounds__(kTile)
+route_scatter(RouteArgs a) {
+    constexpr int WARPS = kTile / 32;
+    __shared__ unsigned int warp_cnt[WARPS][kMaxExperts];
+    __shared__ unsigned int warp_base[WARPS][kMaxExperts];
+    const unsigned E = static_cast<unsigned>(a.E);
+    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const std::size_t t = static_cast<std::size_t>(blockIdx.x) * kTile + threadIdx.x;
+    const bool valid = t < a.T;
+    unsigned e0 = 0xFFu, e1 = 0xFFu;
+    if (valid) {
+        const unsigned short pair = reinterpret_cast<const unsigned short*>(a.routes)[t];
+        e0 = pair & 0xFFu;
+        e1 = pair >> 8;
+    }
+    unsigned my_mask = 0;
+    for (unsigned e = 0; e < E; ++e) {
+        const unsigned m = __ballot_sync(0xffffffffu, valid && (e0 == e || e1 == e));
+        if (lane == e) my_mask = m;
+        if (lane == 0) warp_cnt[warp][e] = __popc(m);
+    }
+    __syncthreads();
+    if (threadIdx.x < E) {
+        const unsigned e = threadIdx.x;
+        unsigned base = __ldg(a.offsets + e) +
+                        a.tile_counts[static_cast<std::size_t>(blockIdx.x) * E + e];
+        for (int w = 0; w < WARPS; ++w) {
+            warp_base[w][e] = base;
+            base += warp_cnt[w][e];
+        }
+    }
+    __syncthreads();
+    const unsigned m0 = __shfl_sync(0xffffffffu, my_mask, e0 & 31u);
+    const unsigned m1 = __shfl_sync(0xffffffffu, my_mask, e1 & 31u);
+    if (valid) {
+        const unsigned lt = (1u << lane) - 1u;
+        const unsigned p0 = warp_base[warp][e0] + __popc(m0 & lt);
+        const unsigned p1 = warp_base[warp][e1] + __popc(m1 & lt);
+        a.assignment_rows[p0] = static_cast<std::uint32_t>(t);
+        a.assignment_rows[p1] = static_cast<std::uint32_t>(t);
+        reinterpret_cast<uint2*>(a.route_positions)[t] = make_uint2(p0, p1);
+    }
+}
+
+// ---- gated SiLU -------------------------------------------------------------
+
+// g / (1 + (float)exp((double)-g)) * u, k_silu_mul (src/tensor.cu:2005-2008).
+__device__ __forceinline__ float silu_mul1(float g, float u) {
+    const float act = __fdiv_rn(g, __fadd_rn(1.0f, static_cast<float>(exp(static_cast<double>(-g)))));
+    return __fmul_rn(act, u);
+}
+
+constexpr int kSiluThreads = 256;
+constexpr int kSiluUnroll = 4;
+
+// One warp per row, 128-bit chunks, up to four chunks in flight per lane.
+__global__ void __launch_bounds__(kSiluThreads)
+silu_mul_vec(const float* __restrict__ gate, std::size_t ldg, const float* __restrict__ up,
+             std::size_t ldu, float* __restrict__ out, std::size_t ldo, std::size_t rows,
+             std::size_t c4) {
+    const unsigned lane = threadIdx.x & 31;
+    const std::size_t warps = static_cast<std::size_t>(gridDim.x) * (kSiluThreads / 32);
+    for (std::size_t r = static_cast<std::size_t>(blockIdx.x) * (kSiluThreads / 32) + (threadIdx.x >> 5);
+         r < rows; r += warps) {
+        const float4* g4 = reinterpret_cast<const float4*>(gate + r * ldg);
+        const float4* u4 = reinterpret_cast<const float4*>(up + r * ldu);
+        float4* o4 = reinterpret_cast<float4*>(out + r * ldo);
+        for (std::size_t j0 = lane; j0 < c4; j0 += 32 * kSiluUnroll) {
+            float4 g[kSiluUnroll], u[kSiluUnroll];
+#pragma unroll
+            for (int k = 0; k < kSiluUnroll; ++k) {
+                const std::size_t j = j0 + 32 * k;
+                if (j < c4) {
+                    g[k] = ld_stream(g4 + j);
+                    u[k] = ld_stream(u4 + j);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kSiluUnroll; ++k) {
+                const std::size_t j = j0 + 32 * k;
+                if (j < c4)
+                    st_plain(o4 + j, make_float4(silu_mul1(g[k].x, u[k].x), silu_mul1(g[k].y, u[k].y),
+                                                 silu_mul1(g[k].z, u[k].z), silu_mul1(g[k].w, u[k].w)));
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kSiluThreads)
+silu_mul_scalar(const float* __restrict__ gate, std::size_t ldg, const float* __restrict__ up,
+                std::size_t ldu, float* __restrict__ out, std::size_t ldo, std::size_t rows,
+                std::size_t cols) {
+    const unsigned lane = threadIdx.x & 31;
+    const std::size_t warps = static_cast<std::size_t>(gridDim.x) * (kSiluThreads / 32);
+    for (std::size_t r = static_cast<std::size_t>(blockIdx.x) * (kSiluThreads / 32) + (threadIdx.x >> 5);
+         r < rows; r += warps)
+        for (std::size_t j = lane; j < cols; j += 32)
+            out[r * ldo + j] = silu_mul1(__ldg(gate + r * ldg + j), __ldg(up + r * ldu + j));
+}
+
+// ---- weighted un-permute ----------------------------------------------------
+
+constexpr int kRowThreads = 256;
+
+template <bool VEC>
+__global__ void __launch_bounds__(kRowThreads)
+moe_combine_rows(const float* __restrict__ expert_out, std::size_t expert_rows,
+                 const std::uint8_t* __restrict__ routes,
+                 const std::uint32_t* __restrict__ route_positions, float* __restrict__ out,
+                 std::size_t T, std::size_t h) {
+    for (std::size_t t = blockIdx.x; t < T; t += gridDim.x) {
+        const CombineRows cr = combine_rows(routes, route_positions, t, expert_rows);
+        if (VEC) {
+            const std::size_t h4 = h / 4;
+            const float4* e4 = reinterpret_cast<const float4*>(expert_out);
+            float4* o4 = reinterpret_cast<float4*>(out) + t * h4;
+            for (std::size_t j0 = threadIdx.x; j0 < h4; j0 += kRowThreads * 4) {
+                float4 lo[4], hi[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const std::size_t j = j0 + static_cast<std::size_t>(k) * kRowThreads;
+                    if (j < h4) {
+                        lo[k] = cr.lo < expert_rows ? ld_stream(e4 + cr.lo * h4 + j) : zero4();
+                        hi[k] = cr.hi < expert_rows ? ld_stream(e4 + cr.hi * h4 + j) : zero4();
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const std::size_t j = j0 + static_cast<std::size_t>(k) * kRowThreads;
+                    if (j < h4) st_plain(o4 + j, combine4(lo[k], hi[k]));
+                }
+            }
+        } else {
+            for (std::size_t j = threadIdx.x; j < h; j += kRowThreads) {
+                const float lo = cr.lo < expert_rows ? __ldg(expert_out + cr.lo * h + j) : 0.0f;
+                const float hi = cr.hi < expert_rows ? __ldg(expert_out + cr.hi * h + j) : 0.0f;
+                out[t * h + j] = combine_one(lo, hi);
+            }
+        }
+    }
+}
+
+// ---- residual add -------------------------------------------------------------
+
+__global__ void __launch_bounds__(256)
+add_vec(float4* __restrict__ a, const float4* __restrict__ b, std::size_t n4) {
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * 256;
+    for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * 256 + threadIdx.x; i < n4; i += stride * 2) {
+        const std::size_t i2 = i + stride;
+        const float4 x0 = ld_plain(a + i), y0 = ld_stream(b + i);
+        float4 x1, y1;
+        if (i2 < n4) {
+            x1 = ld_plain(a + i2);
+            y1 = ld_stream(b + i2);
+        }
+        st_plain(a + i, add4(x0, y0));
+        if (i2 < n4) st_plain(a + i2, add4(x1, y1));
+    }
+}
+
+__global__ void __launch_bounds__(256)
+add_scalar(float* __restrict__ a, const float* __restrict__ b, std::size_t n) {
+    const std::size_t stride = static_cast<std::size_t>(gridDim.x) * 256;
+    for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * 256 + threadIdx.x; i < n; i += stride)
+        a[i] = __fadd_rn(a[i], b[i]);
+}
+
+std::size_t route_tiles(std::size_t T) { return (T + kTile - 1) / kTile; }
+
+}  // namespace
+}  // namespace b2
+
+B2_DEFINE_CHECK_TAKER(moe)
+
+extern "C" {
+
+int b2_moe_route_workspace_size(size_t T, size_t E, size_t* bytes) {
+    if (!bytes) return b2::invalid("b2_moe_route_workspace_size: null bytes");
+    *bytes = b2::kWsHeader + b2::route_tiles(T) * E * sizeof(uint32_t);
+    return B2_OK;
+}
+
+int b2_moe_route(const float* logits, size_t T, size_t E, float quantum, float tie_eps,
+                 uint8_t* routes, uint32_t* counts, uint32_t* offsets, uint32_t* assignment_rows,
+                 uint32_t* route_positions, uint32_t* work_expert64, uint32_t* work_start64,
+                 uint32_t* work_expert128, uint32_t* work_start128, void* workspace,
+                 size_t workspace_bytes, b2_stream_t stream) {
+    using namespace b2;
+    if (E < 2 || E > static_cast<size_t>(kMaxExperts))
+        return invalid("b2_moe_route: E must be in [2, 32]");
+    if (T == 0) return B2_OK;
+    if (T > 0x7FFFFFFFu) return invalid("b2_moe_route: T too large for uint32 positions");
+    if (!logits || !routes || !counts || !offsets || !assignment_rows || !route_positions || !workspace)
+        return invalid("b2_moe_route: null pointer");
+    size_t need = 0;
+    b2_moe_route_workspace_size(T, E, &need);
+    if (workspace_bytes < need) return invalid("b2_moe_route: workspace too small");
+    if ((reinterpret_cast<std::uintptr_t>(routes) & 1u) || (reinterpret_cast<std::uintptr_t>(route_positions) & 7u) ||
+        (reinterpret_cast<std::uintptr_t>(workspace) & 15u))
+        return invalid("b2_moe_route: misaligned routes / route_positions / workspace");
+    RouteArgs a{};
+    a.logits = logits; a.T = T; a.E = E; a.quantum = quantum; a.tie_eps = tie_eps;
+    a.routes = routes; a.counts = counts; a.offsets = offsets;
+    a.assignment_rows = assignment_rows; a.route_positions = route_positions;
+    a.we64 = work_expert64; a.ws64 = work_start64; a.we128 = work_expert128; a.ws128 = work_start128;
+    a.ticket = static_cast<uint32_t*>(workspace);
+    a.tile_counts = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + kWsHeader);
+    a.tiles = route_tiles(T);
+    if (a.tiles > 0x7FFFFFFFu) return invalid("b2_moe_route: too many tiles");
+    cudaStream_t s = as_stream(stream);
+    route_select<<<static_cast<unsigned>(a.tiles), kTile, 0, s>>>(a);
+    route_scatter<<<static_cast<unsigned>(a.tiles), kTile, 0, s>>>(a);
+    return launch_result("b2_moe_route");
+}
+
+int b2_silu_mul(const float* gate, size_t ld_gate, const float* up, size_t ld_up, float* out,
+                size_t ld_out, size_t rows, size_t cols, b2_stream_t stream) {
+    using namespace b2;
+    if (rows == 0 || cols == 0) return B2_OK;
+    if (!gate || !up || !out) return invalid("silu_mul: null pointer");
+    if (ld_gate < cols || ld_up < cols || ld_out < cols) return invalid("silu_mul shape");
+    cudaStream_t s = as_stream(stream);
+    const bool vec = (cols % 4) == 0 && (ld_gate % 4) == 0 && (ld_up % 4) == 0 && (ld_out % 4) == 0 &&
+                     aligned16(gate) && aligned16(up) && aligned16(out);
+    const std::size_t blocks_needed = (rows + (kSiluThreads / 32) - 1) / (kSiluThreads / 32);
+    if (vec) {
+        const unsigned grid = wave_grid(reinterpret_cast<const void*>(silu_mul_vec), kSiluThreads, 0, blocks_needed);
+        silu_mul_vec<<<grid, kSiluThreads, 0, s>>>(gate, ld_gate, up, ld_up, out, ld_out, rows, cols / 4);
+    } else {
+        const unsigned grid = wave_grid(reinterpret_cast<const void*>(silu_mul_scalar), kSiluThreads, 0, blocks_needed);
+        silu_mul_scalar<<<grid, kSiluThreads, 0, s>>>(gate, ld_gate, up, ld_up, out, ld_out, rows, cols);
+    }
+    return launch_result("b2_silu_mul");
+}
+
+int b2_moe_combine(const float* expert_out, size_t expert_rows, const uint8_t* routes,
+                   const uint32_t* route_positions, float* out, size_t T, size_t h,
+                   b2_stream_t stream) {
+    using namespace b2;
+    if (T == 0) return B2_OK;
+    if (!expert_out || !routes || !route_positions || !out) return invalid("moe combine: null pointer");
+    if (h == 0) return invalid("moe combine shape");
+    cudaStream_t s = as_stream(stream);
+    if ((h % 4) == 0 && aligned16(expert_out) && aligned16(out)) {
+        const unsigned grid = wave_grid(reinterpret_cast<const void*>(moe_combine_rows<true>), kRowThreads, 0, T);
+        moe_combine_rows<true><<<grid, kRowThreads, 0, s>>>(expert_out, expert_rows, routes, route_positions, out, T, h);
+    } else {
+        const unsigned grid = wave_grid(reinterpret_cast<const void*>(moe_combine_rows<false>), kRowThreads, 0, T);
+        moe_combine_rows<false><<<grid, kRowThreads, 0, s>>>(expert_out, expert_rows, routes, route_positions, out, T, h);
+    }
+    return launch_result("b2_moe_combine");
+}
+
+int b2_add(float* a, const float* b, size_t n, b2_stream_t stream) {
+    using namespace b2;
+    if (n == 0) return B2_OK;
+    if (!a || !b) return invalid("add: null pointer");
+    cudaStream_t s = as_stream(stream);
+    if ((n % 4) == 0 && aligned16(a) && aligned16(b)) {
+        const std::size_t n4 = n / 4;
+        const unsigned grid = wave_grid(reinterpret_cast<const void*>(add_vec), 256, 0, (n4 + 511) / 512);
+        add_vec<<<grid, 256, 0, s>>>(reinterpret_cast<float4*>(a), reinterpret_cast<const float4*>(b), n4);
+    } else {
+        const unsigned grid = wave_grid(reinterpret_cast<const void*>(add_scalar), 256, 0, (n + 255) / 256);
+        add_scalar<<<grid, 256, 0, s>>>(a, b, n);
+    }
+    return launch_result("b2_add");
+}
+
+}  // extern "C"

@@ -1,0 +1,260 @@
+/*
+ * aps2026_b200.h -- C ABI of the B200 (sm_100a) non-GEMM prefill layer ops of
+ * Phi-tiny-MoE: embedding gather, LayerNorm (+ fused residual add), RoPE on
+ * Q/K, causal scaled softmax, deterministic top-2 routing with the
+ * token->expert permutation, gated SiLU, weighted un-permute, residual add,
+ * and the prefix-trie dedup that feeds them.
+ *
+ * The reference exposes these as C++ free functions in `namespace tensor_ops`
+ * that take `Tensor&` (ezzy0654/aps2026 include/tensor.h:63-161). This ABI
+ * replaces each of them with a plain-C entry point:
+ *   - every tensor is a raw DEVICE pointer (row-major, fp32 unless noted) plus
+ *     explicit sizes -- shapes that the reference read from Tensor::size();
+ *   - every device entry point takes the stream to run on (NULL = legacy
+ *     default stream, which is what the reference always used);
+ *   - nothing allocates device memory; scratch is caller-provided and sized by
+ *     a *_workspace_size() query;
+ *   - there is no hidden per-process state except one status word per device
+ *     that in-kernel bounds checks write (b2_device_status), so one host
+ *     thread per GPU may call concurrently on different devices/streams;
+ *   - errors are status codes instead of the reference's exceptions:
+ *     B2_ERR_INVALID_ARGUMENT where the reference throws
+ *     std::invalid_argument, B2_ERR_CUDA where its check_cuda throws
+ *     std::runtime_error (src/tensor.cu:370-374). b2_last_error() returns the
+ *     message of the calling thread's last failure.
+ *
+ * Floating point: by default reductions (LayerNorm moments, softmax
+ * denominators) are tree-shaped and agree with the reference kernels within
+ * 1e-5 relative OR 1e-6 absolute. With B2_FLAG_EXACT_ORDER they are
+ * evaluated in the reference's serial ascending order and agree bit for bit.
+ * Index/integer outputs (gather, routing, permutation) are always bit-exact.
+ */
+#ifndef APS2026_B200_H
+#define APS2026_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t passed as an opaque pointer; NULL selects stream 0. */
+typedef void* b2_stream_t;
+
+enum b2_status {
+    B2_OK = 0,
+    B2_ERR_INVALID_ARGUMENT = 1, /* bad shape / size / null / alignment      */
+    B2_ERR_CUDA = 2,             /* kernel launch or CUDA runtime failure     */
+    B2_ERR_DEVICE_CHECK = 3,     /* an in-kernel bounds check saw a bad index */
+    B2_ERR_TIMEOUT = 4,          /* a bounded device wait gave up             */
+    B2_ERR_UNSUPPORTED = 5       /* valid request outside what is built       */
+};
+
+/* Flags for the floating-point reductions. */
+#define B2_FLAG_EXACT_ORDER 1u /* serial ascending sums, bit-exact to reference */
+
+/* ---- library / status ---------------------------------------------------- */
+
+/* Version string of the library ("aps2026_b200 <semver> sm_100a"). */
+const char* b2_version(void);
+
+/* Message of this thread's last non-OK status ("" if none). */
+const char* b2_last_error(void);
+
+/*
+ * Reads, then clears, the current device's in-kernel check word. Waits for
+ * `stream` first. *status_out is 0 when no kernel since the last call saw an
+ * out-of-range index; otherwise a bitmask of B2_CHECK_* (which kernel
+ * family). Kernels that see a bad index skip that access (their output for
+ * that row is zero) instead of reading out of bounds.
+ */
+#define B2_CHECK_GATHER 1u
+#define B2_CHECK_ROPE 2u
+#define B2_CHECK_COMBINE 4u
+#define B2_CHECK_ATTENTION 8u
+int b2_device_status(uint32_t* status_out, b2_stream_t stream);
+
+/* ---- embedding / row gather ---------------------------------------------- */
+
+/*
+ * out[i, :] = x[rows[i], :] for i < count; x is [x_rows, h], out [count, h],
+ * rows a device uint32 array. Bit-exact copy.
+ * Replaces tensor_ops::gather_rows_gpu (include/tensor.h:115-116 and :138;
+ * src/tensor.cu:3379-3387, :3419-3426; kernel k_gather_rows :2635-2642).
+ * count == 0 is a no-op (as the RowIndexBuffer overload, :3420).
+ */
+int b2_gather_rows(const float* x, size_t x_rows, size_t h,
+                   const uint32_t* rows, size_t count, float* out,
+                   b2_stream_t stream);
+
+/* ---- LayerNorm ------------------------------------------------------------ */
+
+/*
+ * y[r, :] = (x[r, :] - mean) * (1 / sqrtf(var + eps)) * gamma + beta, with
+ * mean and var the two-pass row moments over h. x, y: [rows, h].
+ * Replaces tensor_ops::layer_norm_gpu (include/tensor.h:86-87;
+ * src/tensor.cu:3262-3280; kernel k_layer_norm :2130-2142).
+ */
+int b2_layer_norm(const float* x, const float* gamma, const float* beta,
+                  float* y, size_t rows, size_t h, float eps, uint32_t flags,
+                  b2_stream_t stream);
+
+/*
+ * x[r, :] += residual[r, :] (written back), then y = LayerNorm(x).
+ * Replaces tensor_ops::add_layer_norm_gpu (include/tensor.h:88-90;
+ * src/tensor.cu:3282-3295; kernel k_add_layer_norm :2144-2178).
+ */
+int b2_add_layer_norm(float* x, const float* residual, const float* gamma,
+                      const float* beta, float* y, size_t rows, size_t h,
+                      float eps, uint32_t flags, b2_stream_t stream);
+
+/*
+ * Fused MoE un-permute + carried residual add + LayerNorm:
+ *   x_out[t, :] = combine(expert_out)[t, :] + carry[t, :]
+ *   y[t, :]     = LayerNorm(x_out[t, :])
+ * where combine is exactly b2_moe_combine. This is the reference's
+ * k_moe_combine (src/tensor.cu:1968-1988) followed by the next layer's
+ * k_add_layer_norm of the carry protocol (src/layer.cu:273-300,
+ * src/model.cu:145-150) in one pass: the MoE output row never goes to HBM.
+ * Same arithmetic in the same order, so it equals the two-call sequence.
+ */
+int b2_moe_combine_add_layer_norm(const float* expert_out, size_t expert_rows,
+                                  const uint8_t* routes,
+                                  const uint32_t* route_positions,
+                                  const float* carry, const float* gamma,
+                                  const float* beta, float* x_out, float* y,
+                                  size_t rows, size_t h, float eps,
+                                  uint32_t flags, b2_stream_t stream);
+
+/* ---- rotary embedding ----------------------------------------------------- */
+
+/*
+ * HOST function. Fills cos_host / sin_host ([max_seq, head_dim/2] floats)
+ * with cos/sin(p * theta^(-2j/head_dim)) evaluated exactly as the
+ * reference's host-built table (src/tensor.cu:2716-2724: powf, cosf, sinf in
+ * float), so the device lookups are bit-identical.
+ */
+int b2_rope_table(size_t max_seq, size_t head_dim, float theta,
+                  float* cos_host, float* sin_host);
+
+/*
+ * Rotate-half RoPE in place on q [rows, q_heads*head_dim] and
+ * k [rows, kv_heads*head_dim] in ONE launch; row r uses table row
+ * row_pos[r] (< table_rows) of the device tables from b2_rope_table.
+ * Replaces tensor_ops::apply_rope_tree_gpu / apply_rope_gpu
+ * (include/tensor.h:91-94, :104-108; src/tensor.cu:3297-3314, :3342-3359;
+ * kernel k_rope :2180-2197, launched twice there).
+ */
+int b2_rope(float* q, float* k, const uint32_t* row_pos, size_t rows,
+            size_t q_heads, size_t kv_heads, size_t head_dim,
+            const float* cos_table, const float* sin_table, size_t table_rows,
+            b2_stream_t stream);
+
+/* ---- causal scaled softmax ------------------------------------------------ */
+
+/*
+ * probs[h, i, j] = softmax_j(scores[h, i, j] * scale) over the causal
+ * sliding window j in [max(0, i + 1 - window), i]; entries outside it are 0.
+ * scores, probs: [heads, T, ld] (ld >= T; columns >= T are not touched).
+ * Max, exp(double) rounded to float, ascending denominator and division are
+ * the softmax section of k_attention_tree_gqa4 (src/tensor.cu:2448, :2526,
+ * :2549-2585; window rule :2435-2439). The reference declares
+ * softmax_last_dim (include/tensor.h:152) but defines no standalone kernel.
+ */
+int b2_causal_softmax(const float* scores, float* probs, size_t heads,
+                      size_t T, size_t ld, float scale, size_t window,
+                      uint32_t flags, b2_stream_t stream);
+
+/* ---- MoE routing (bit-exact) ---------------------------------------------- */
+
+/* Bytes of caller workspace b2_moe_route needs for T tokens, E experts. */
+int b2_moe_route_workspace_size(size_t T, size_t E, size_t* bytes);
+
+/*
+ * Top-2 routing + token->expert permutation, replacing the routing part of
+ * tensor_ops::moe_forward_grouped_gpu (include/tensor.h:146-147;
+ * src/tensor.cu:2790-2821: memsets, k_moe_top2 :1293-1331,
+ * k_moe_offsets_work :1337-1374, k_moe_fill_stable :1376-1418).
+ *   logits            [T, E] fp32 (E <= 32)
+ *   routes            [T, 2] uint8: first, second expert of each token
+ *   counts            [E]    tokens per expert
+ *   offsets           [E+1]  exclusive prefix of counts
+ *   assignment_rows   [2T]   token of each expert-ordered assignment
+ *   route_positions   [2T]   position of (token t, slot s) at [2t+s]
+ *   work_expert64 / work_start64    [ceil(2T/64)+E]  64-row chunks
+ *   work_expert128 / work_start128  [ceil(2T/128)+E] 128-row chunks
+ *     (unused queue entries are 0xFFFFFFFF, as the reference memsets them;
+ *      any queue pointer may be NULL to skip it)
+ * Scores are quantized to `quantum` (reference 1e-3) and picked by an
+ * ascending scan that only replaces on > best + tie_eps (reference 2e-2).
+ * The workspace (b2_moe_route_workspace_size bytes) must be zero-filled
+ * before its first use; each call leaves it zero-filled again.
+ */
+int b2_moe_route(const float* logits, size_t T, size_t E, float quantum,
+                 float tie_eps, uint8_t* routes, uint32_t* counts,
+                 uint32_t* offsets, uint32_t* assignment_rows,
+                 uint32_t* route_positions, uint32_t* work_expert64,
+                 uint32_t* work_start64, uint32_t* work_expert128,
+                 uint32_t* work_start128, void* workspace,
+                 size_t workspace_bytes, b2_stream_t stream);
+
+/* ---- expert activation, un-permute, residual ------------------------------ */
+
+/*
+ * out[r, c] = g / (1 + (float)exp((double)-g)) * up[r, c], g = gate[r, c];
+ * gate/up/out rows strided by ld_gate/ld_up/ld_out elements, so both the
+ * split [2T,448] and the concatenated [2T,896] gate|up layouts work.
+ * Replaces tensor_ops::silu_mul_gpu (include/tensor.h:85;
+ * src/tensor.cu:3254-3260; kernel k_silu_mul :2001-2010; the same math is
+ * the epilogue of k_moe_pair_silu_8x8 :1953-1965).
+ */
+int b2_silu_mul(const float* gate, size_t ld_gate, const float* up,
+                size_t ld_up, float* out, size_t ld_out, size_t rows,
+                size_t cols, b2_stream_t stream);
+
+/*
+ * out[t, :] = 0.5 * expert_out[p_lo, :] + 0.5 * expert_out[p_hi, :], where
+ * p_lo/p_hi are the route_positions of token t's two assignments in
+ * ascending EXPERT id order; expert_out is [expert_rows, h].
+ * Replaces k_moe_combine (src/tensor.cu:1968-1988, launched at :2922-2926).
+ */
+int b2_moe_combine(const float* expert_out, size_t expert_rows,
+                   const uint8_t* routes, const uint32_t* route_positions,
+                   float* out, size_t T, size_t h, b2_stream_t stream);
+
+/*
+ * a[i] += b[i] for i < n.
+ * Replaces tensor_ops::add_inplace_gpu (include/tensor.h:83;
+ * src/tensor.cu:3236-3242; kernel k_add :1990-1993).
+ */
+int b2_add(float* a, const float* b, size_t n, b2_stream_t stream);
+
+/* ---- prefix-trie dedup (host) --------------------------------------------- */
+
+/*
+ * HOST function. Builds the prefix trie of `batch` prompts packed in `ids`
+ * (prompt b has seq_lens[b] tokens, all in [0, vocab)), numbering nodes in
+ * order of creation exactly as PhiTinyMoEModel::generate does
+ * (src/model.cu:64-117):
+ *   token_node [sum(seq_lens)] node of each packed token row
+ *   node_token [nodes]  token id of each node        (capacity: total tokens)
+ *   node_depth [nodes]  depth = RoPE position        (capacity: total tokens)
+ *   node_anc   [nodes * anc_stride] ancestor chain root->node, zero padded;
+ *              may be NULL (it only feeds the attention core)
+ * *nodes_out receives the node count. anc_stride must be >= max seq_len.
+ * Returns B2_ERR_INVALID_ARGUMENT for an empty batch or prompt, a token out
+ * of the vocabulary, or a prompt longer than max_len (the reference's
+ * MAX_POSITION_EMBEDDINGS check, src/model.cu:55-58).
+ */
+int b2_prefix_trie_build(const int32_t* ids, const uint32_t* seq_lens,
+                         size_t batch, size_t vocab, size_t max_len,
+                         uint32_t* token_node, uint32_t* node_token,
+                         uint32_t* node_depth, uint32_t* node_anc,
+                         size_t anc_stride, size_t* nodes_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* APS2026_B200_H */
