@@ -54,6 +54,15 @@ inline unsigned wave_grid(const void* kernel, int threads, std::size_t smem,
     return static_cast<unsigned>(g);
 }
 
+// Allows `kernel` to launch with `bytes` of dynamic shared memory: above the
+// 48 KB default (static shared memory counts against it too) the opt-in
+// attribute must be raised first.
+inline cudaError_t allow_dynamic_smem(const void* kernel, std::size_t bytes) {
+    if (bytes <= 40 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(bytes));
+}
+
 // ---- in-kernel bounds checks -------------------------------------------------
 //
 // Every kernel that dereferences a caller-provided index checks it, skips

@@ -255,9 +255,7 @@ template <int MODE, int THREADS, int V, bool EXACT>
 int launch_reg(const LnArgs& a, cudaStream_t s) {
     const std::size_t smem = EXACT ? a.h * sizeof(float) : 0;
     auto kernel = ln_rows_reg<MODE, THREADS, V, EXACT>;
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
+    if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("layer norm: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), THREADS, smem, a.rows);
     kernel<<<grid, THREADS, smem, s>>>(a);
@@ -268,9 +266,7 @@ template <int MODE, bool EXACT>
 int launch_smem(const LnArgs& a, cudaStream_t s) {
     const std::size_t smem = a.h * sizeof(float);
     auto kernel = ln_rows_smem<MODE, EXACT>;
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
+    if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("layer norm: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), 256, smem, a.rows);
     kernel<<<grid, 256, smem, s>>>(a);

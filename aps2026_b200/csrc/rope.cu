@@ -23,10 +23,11 @@ namespace {
 constexpr int kRopeRowsPerStep = 2;
 
 // out0 = x0 * c - x1 * s, out1 = x1 * c + x0 * s, with the multiply-adds
-// fused the way nvcc fuses the reference's expressions.
+// fused the way nvcc fuses the reference's expressions in k_rope:
+// fma(x0, c, -(x1 * s)) and fma(x0, s, x1 * c).
 __device__ __forceinline__ void rotate(float& x0, float& x1, float c, float s) {
     const float a = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
-    const float b = __fmaf_rn(x1, c, __fmul_rn(x0, s));
+    const float b = __fmaf_rn(x0, s, __fmul_rn(x1, c));
     x0 = a;
     x1 = b;
 }

@@ -160,9 +160,7 @@ template <int V, bool EXACT>
 int launch_reg(const SoftmaxArgs& a, cudaStream_t s) {
     const std::size_t smem = EXACT ? a.T * sizeof(float) : 0;
     auto kernel = causal_softmax_reg<V, EXACT>;
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
+    if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("causal softmax: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), kSmThreads, smem, a.rows);
     kernel<<<grid, kSmThreads, smem, s>>>(a);
@@ -173,9 +171,7 @@ template <bool EXACT>
 int launch_smem(const SoftmaxArgs& a, cudaStream_t s) {
     const std::size_t smem = a.T * sizeof(float);
     auto kernel = causal_softmax_smem<EXACT>;
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
+    if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("causal softmax: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), kSmThreads, smem, a.rows);
     kernel<<<grid, kSmThreads, smem, s>>>(a);

@@ -1,0 +1,291 @@
+"""Non-GEMM prefill pipeline: prefix-trie dedup, the per-layer op sequence of
+PhiDecoderLayer::forward_carry over all layers, the final add + LayerNorm,
+and prompt sharding across GPUs with one NCCL gather of the final hidden
+states.
+
+The GEMM outputs of each layer (q/k projections, attention + o_proj, router
+logits, expert gate/up and W2 outputs) are supplied as seeded stand-in
+tensors of the config.h shapes (``StandIns``): the projections are outside
+this path. Everything on the path itself runs through the C ABI
+(``b2_prefill_layers`` for the layer loop, ``b2_prefix_trie_build`` for the
+trie, ``b2_gather_rows`` for the expansion back to token rows).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from . import _lib, ops
+
+VOCAB = 32064
+HIDDEN = 4096
+LAYERS = 32
+Q_HEADS = 16
+KV_HEADS = 4
+HEAD_DIM = 128
+EXPERTS = 16
+INTER = 448
+MAX_POS = 4096
+
+
+class Shape(C.Structure):
+    _fields_ = [("rows", C.c_size_t), ("hidden", C.c_size_t), ("q_heads", C.c_size_t),
+                ("kv_heads", C.c_size_t), ("head_dim", C.c_size_t), ("experts", C.c_size_t),
+                ("intermediate", C.c_size_t), ("eps", C.c_float), ("router_quantum", C.c_float),
+                ("router_tie_eps", C.c_float), ("flags", C.c_uint32)]
+
+
+class Layer(C.Structure):
+    _fields_ = [("q", C.c_void_p), ("k", C.c_void_p), ("attn", C.c_void_p), ("router_logits", C.c_void_p),
+                ("gate", C.c_void_p), ("up", C.c_void_p), ("ld_gate_up", C.c_size_t),
+                ("expert_out", C.c_void_p), ("ln1_gamma", C.c_void_p), ("ln1_beta", C.c_void_p),
+                ("ln2_gamma", C.c_void_p), ("ln2_beta", C.c_void_p)]
+
+
+class Work(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("x", "normed", "post", "act", "routes", "counts", "offsets",
+                                          "assignment_rows", "route_positions", "work_expert64",
+                                          "work_start64", "work_expert128", "work_start128", "route_ws")] + [
+        ("route_ws_bytes", C.c_size_t)]
+
+
+def launches_per_run(layers: int) -> int:
+    """Kernel launches of one b2_prefill_layers call (B2_PREFILL_LAUNCHES):
+    gather + LN0 + per layer RoPE, add+LN, routing (2 kernels), SiLU, and the
+    31 + 1 fused un-permute + add + LN launches."""
+    return 2 + 6 * layers
+
+
+# ---- synthetic inputs (BASELINE configs 4 and 5) -------------------------------------
+
+
+def prompts_config4(seed: int = 3, batch: int = 16, length: int = 1024, shared: int = 256) -> list[np.ndarray]:
+    """16 prompts x 1024 tokens whose first 256 tokens are identical; ids
+    uniform over the vocabulary."""
+    g = np.random.default_rng(seed)
+    prefix = g.integers(0, VOCAB, shared)
+    return [np.concatenate([prefix, g.integers(0, VOCAB, length - shared)]).astype(np.int32) for _ in range(batch)]
+
+
+def prompts_config5(seed: int = 4, batch: int = 64, length: int = 2048) -> list[np.ndarray]:
+    """64 prompts x 2048 tokens, ids uniform over the vocabulary."""
+    g = np.random.default_rng(seed)
+    return [g.integers(0, VOCAB, length).astype(np.int32) for _ in range(batch)]
+
+
+def _randn(shape, gen, device, mean=0.0, std=1.0):
+    t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
+    if std != 1.0:
+        t.mul_(std)
+    if mean != 0.0:
+        t.add_(mean)
+    return t
+
+
+@dataclass
+class Weights:
+    """Embedding table and LayerNorm parameters (random init of the
+    architecture: emb ~ N(0, 0.02), gamma ~ N(1, 0.1), beta ~ N(0, 0.1))."""
+    emb: torch.Tensor
+    ln1: list  # [(gamma, beta)] per layer (input_layernorm)
+    ln2: list  # post_attention_layernorm
+    final: tuple
+
+    @staticmethod
+    def make(device, seed: int, layers: int = LAYERS, vocab: int = VOCAB, hidden: int = HIDDEN) -> "Weights":
+        gen = torch.Generator(device=device).manual_seed(seed)
+        emb = _randn((vocab, hidden), gen, device, std=0.02)
+        ln = lambda: (_randn(hidden, gen, device, 1.0, 0.1), _randn(hidden, gen, device, 0.0, 0.1))  # noqa: E731
+        return Weights(emb, [ln() for _ in range(layers)], [ln() for _ in range(layers)], ln())
+
+
+@dataclass
+class StandIns:
+    """Seeded N(0,1) stand-ins for one layer's GEMM outputs (config.h shapes)."""
+    q: torch.Tensor           # [rows, q_heads*head_dim]
+    k: torch.Tensor           # [rows, kv_heads*head_dim]
+    attn: torch.Tensor        # [rows, hidden]
+    logits: torch.Tensor      # [rows, experts]
+    gate_up: torch.Tensor     # [2*rows, 2*intermediate]: gate | up per row
+    expert_out: torch.Tensor  # [2*rows, hidden]
+
+    @staticmethod
+    def make(rows: int, device, gen, hidden=HIDDEN, q_heads=Q_HEADS, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
+             experts=EXPERTS, inter=INTER) -> "StandIns":
+        return StandIns(_randn((rows, q_heads * head_dim), gen, device), _randn((rows, kv_heads * head_dim), gen, device),
+                        _randn((rows, hidden), gen, device), _randn((rows, experts), gen, device),
+                        _randn((2 * rows, 2 * inter), gen, device), _randn((2 * rows, hidden), gen, device))
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * 4 for t in (self.q, self.k, self.attn, self.logits, self.gate_up, self.expert_out))
+
+
+def standin_bytes(rows: int) -> int:
+    return 4 * rows * (Q_HEADS * HEAD_DIM + KV_HEADS * HEAD_DIM + HIDDEN + EXPERTS + 2 * 2 * INTER + 2 * HIDDEN)
+
+
+# ---- the batch on one GPU ------------------------------------------------------------------
+
+
+@dataclass
+class Batch:
+    """A prompt batch deduplicated onto prefix-trie nodes, with its index
+    arrays on the device."""
+    prompts: list
+    trie: ops.PrefixTrie
+    node_token: torch.Tensor    # int32 [nodes] on device
+    node_depth: torch.Tensor    # int32 [nodes]
+    token_node: torch.Tensor    # int32 [tokens]
+    last_rows: torch.Tensor     # int32 [batch]: node of each prompt's last token
+    max_len: int
+
+    @property
+    def rows(self) -> int:
+        return self.trie.nodes
+
+    @property
+    def tokens(self) -> int:
+        return int(self.trie.token_node.size)
+
+    @staticmethod
+    def build(prompts: Sequence[np.ndarray], device, pinned: bool = False, stream=None) -> "Batch":
+        trie = ops.prefix_trie(prompts)
+        lens = np.array([len(p) for p in prompts])
+        ends = np.cumsum(lens) - 1
+        last = trie.token_node[ends].astype(np.int32)
+
+        def up(a):
+            t = torch.from_numpy(a.view(np.int32))
+            if pinned:
+                t = t.pin_memory()
+            return t.to(device, non_blocking=pinned)
+
+        return Batch(list(prompts), trie, up(trie.node_token), up(trie.node_depth), up(trie.token_node),
+                     up(last), int(lens.max()))
+
+
+class Pipeline:
+    """Owns the working buffers of one GPU's share of the batch and runs the
+    non-GEMM layer loop through ``b2_prefill_layers``."""
+
+    def __init__(self, batch: Batch, weights: Weights, device, exact: bool = False,
+                 hidden=HIDDEN, q_heads=Q_HEADS, kv_heads=KV_HEADS, head_dim=HEAD_DIM, experts=EXPERTS,
+                 inter=INTER, eps=1e-5):
+        self.batch, self.weights, self.device = batch, weights, device
+        R = batch.rows
+        self.shape = Shape(R, hidden, q_heads, kv_heads, head_dim, experts, inter, eps, ops.ROUTER_SCORE_QUANTUM,
+                           ops.ROUTER_TIE_EPS, ops.B2_FLAG_EXACT_ORDER if exact else 0)
+        e = lambda *s, dt=torch.float32: torch.empty(s, dtype=dt, device=device)  # noqa: E731
+        self.x, self.normed, self.post = e(R, hidden), e(R, hidden), e(R, hidden)
+        self.act = e(2 * R, inter)
+        self.final_x, self.final_out = e(R, hidden), e(R, hidden)
+        self.routing = ops.alloc_routing(R, experts, device)
+        self.route_ws = ops.RouteWorkspace(R, experts, device)
+        self.cos, self.sin = ops.rope_table_gpu(max(batch.max_len, 1), head_dim, ops.ROPE_THETA, device)
+        r = self.routing
+        self.work = Work(self.x.data_ptr(), self.normed.data_ptr(), self.post.data_ptr(), self.act.data_ptr(),
+                         r.routes.data_ptr(), r.counts.data_ptr(), r.offsets.data_ptr(), r.assignment_rows.data_ptr(),
+                         r.route_positions.data_ptr(), r.work_expert64.data_ptr(), r.work_start64.data_ptr(),
+                         r.work_expert128.data_ptr(), r.work_start128.data_ptr(), self.route_ws.buf.data_ptr(),
+                         self.route_ws.bytes)
+        self._fn = _lib.lib().b2_prefill_layers
+        self._layers = None
+        self._layer_key = None
+
+    def bind_layers(self, standins: Sequence[StandIns], layers: int | None = None) -> None:
+        """Layer l uses stand-in set standins[l % len(standins)]."""
+        layers = layers or len(self.weights.ln1)
+        w = self.weights
+        arr = (Layer * layers)()
+        for l in range(layers):
+            s = standins[l % len(standins)]
+            inter = self.shape.intermediate
+            arr[l] = Layer(s.q.data_ptr(), s.k.data_ptr(), s.attn.data_ptr(), s.logits.data_ptr(),
+                           s.gate_up.data_ptr(), s.gate_up.data_ptr() + 4 * inter, s.gate_up.stride(0),
+                           s.expert_out.data_ptr(), w.ln1[l][0].data_ptr(), w.ln1[l][1].data_ptr(),
+                           w.ln2[l][0].data_ptr(), w.ln2[l][1].data_ptr())
+        self._layers = arr
+        self._standins = list(standins)
+
+    def run(self, stream=None, timer: "StageTimer | None" = None) -> None:
+        """Enqueues all layers + the final LayerNorm on `stream` (default:
+        the current torch stream); `timer` records per-launch events."""
+        if self._layers is None:
+            raise RuntimeError("bind_layers() first")
+        st = stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        w = self.weights
+        ev = timer.handles() if timer is not None else None
+        rc = self._fn(C.addressof(self.shape), w.emb.data_ptr(), w.emb.shape[0], self.batch.node_token.data_ptr(),
+                      self.batch.node_depth.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0],
+                      C.addressof(self._layers), len(self._layers), w.final[0].data_ptr(), w.final[1].data_ptr(),
+                      C.addressof(self.work), self.final_x.data_ptr(), self.final_out.data_ptr(),
+                      C.addressof(ev) if ev is not None else None, st)
+        ops._check(rc, "b2_prefill_layers")
+
+    def expand_to_tokens(self, out: torch.Tensor) -> None:
+        """Final hidden states of every token row: out[t] = final_out[token_node[t]]."""
+        ops.gather_rows_gpu(self.final_out, self.batch.token_node, out)
+
+    def last_token_rows(self, out: torch.Tensor) -> None:
+        """Final hidden state of each prompt's last token (the lm_head input)."""
+        ops.gather_rows_gpu(self.final_out, self.batch.last_rows, out)
+
+
+class StageTimer:
+    """CUDA event pairs around every launch of one b2_prefill_layers call
+    (layout of the events argument in include/aps2026_b200.h)."""
+
+    STAGES = ("rope", "add_ln", "route", "silu")
+
+    def __init__(self, layers: int):
+        self.layers = layers
+        self.events = [torch.cuda.Event(enable_timing=True) for _ in range(2 * (5 * layers + 1))]
+        for e in self.events:  # materialise the driver events
+            e.record()
+        torch.cuda.synchronize()
+        self._arr = (C.c_void_p * len(self.events))(*[e.cuda_event for e in self.events])
+
+    def handles(self):
+        return self._arr
+
+    def _ms(self, pair: int) -> float:
+        return self.events[2 * pair].elapsed_time(self.events[2 * pair + 1])
+
+    def durations(self) -> dict:
+        """ms per launch kind after the run has completed: 'ln0', 'fused'
+        (layers 1..L-1 and the final step), and the four per-layer stages."""
+        L = self.layers
+        out = {"ln0": [self._ms(0)], "fused": [self._ms(l) for l in range(1, L + 1)]}
+        for s, name in enumerate(self.STAGES):
+            out[name] = [self._ms(L + 1 + 4 * l + s) for l in range(L)]
+        return out
+
+
+# ---- algorithmic bytes (per trie-node row) ----------------------------------------------------
+
+
+def bytes_per_row(layers: int = LAYERS, hidden=HIDDEN, q_heads=Q_HEADS, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
+                  experts=EXPERTS, inter=INTER) -> dict:
+    """Bytes each kernel of the pipeline must move per node row (each tensor
+    read or written once):
+      gather 2h*4; LN h*4*2; fused un-permute+add+LN: 2 expert rows + carry
+      read, x + normed written = 5h*4 plus 2 route ids + 2 positions;
+      RoPE 2*(q+k)*4; add+LN 4h*4; routing E*4 logits + 2 route ids + 2*4
+      positions + 2*4 assignment rows; SiLU 2 assignments * inter * 12."""
+    f = 4
+    d = dict(
+        gather=2 * hidden * f,
+        ln0=2 * hidden * f,
+        fused=5 * hidden * f + 2 + 2 * 4,
+        rope=2 * (q_heads + kv_heads) * head_dim * f,
+        add_ln=4 * hidden * f,
+        route=experts * f + 2 + 2 * 4 + 2 * 4,
+        silu=2 * inter * 3 * f,
+    )
+    d["total"] = (d["gather"] + d["ln0"] + layers * (d["rope"] + d["add_ln"] + d["route"] + d["silu"])
+                  + layers * d["fused"])
+    return d

@@ -253,6 +253,88 @@ int b2_prefix_trie_build(const int32_t* ids, const uint32_t* seq_lens,
                          uint32_t* node_depth, uint32_t* node_anc,
                          size_t anc_stride, size_t* nodes_out);
 
+/* ---- non-GEMM layer pipeline ------------------------------------------------ */
+
+/* Model shape and numerics of one prefill batch (config.h defaults in
+ * brackets: include/config.h:6-26). */
+typedef struct b2_prefill_shape {
+    size_t rows;          /* trie-node rows of the batch                  */
+    size_t hidden;        /* [4096]                                       */
+    size_t q_heads;       /* [16]                                         */
+    size_t kv_heads;      /* [4]                                          */
+    size_t head_dim;      /* [128]                                        */
+    size_t experts;       /* [16]                                         */
+    size_t intermediate;  /* [448]                                        */
+    float eps;            /* [1e-5]                                       */
+    float router_quantum; /* [1e-3]                                       */
+    float router_tie_eps; /* [2e-2]                                       */
+    uint32_t flags;       /* B2_FLAG_EXACT_ORDER or 0                     */
+} b2_prefill_shape;
+
+/* One decoder layer's GEMM outputs (device pointers; in the real model the
+ * projections and experts write them) and LayerNorm parameters. */
+typedef struct b2_prefill_layer {
+    float* q;                   /* [rows, q_heads*head_dim], RoPE in place   */
+    float* k;                   /* [rows, kv_heads*head_dim], RoPE in place  */
+    float* attn;                /* [rows, hidden] o_proj output; += x in     */
+                                /* place, then carried to the next layer     */
+    const float* router_logits; /* [rows, experts]                           */
+    const float* gate;          /* [2*rows, .] rows strided by ld_gate_up    */
+    const float* up;            /* [2*rows, .]                               */
+    size_t ld_gate_up;
+    const float* expert_out;    /* [2*rows, hidden] W2 output, expert order  */
+    const float* ln1_gamma;     /* input_layernorm [hidden]                  */
+    const float* ln1_beta;
+    const float* ln2_gamma;     /* post_attention_layernorm [hidden]         */
+    const float* ln2_beta;
+} b2_prefill_layer;
+
+/* Caller-owned working buffers (nothing is allocated by the library). */
+typedef struct b2_prefill_work {
+    float* x;                   /* [rows, hidden] residual stream            */
+    float* normed;              /* [rows, hidden] input LN out (-> q/k/v)     */
+    float* post;                /* [rows, hidden] post-attn LN out (-> MoE)   */
+    float* act;                 /* [2*rows, intermediate] SiLU(gate)*up       */
+    uint8_t* routes;            /* b2_moe_route outputs, sized for rows       */
+    uint32_t* counts;
+    uint32_t* offsets;
+    uint32_t* assignment_rows;
+    uint32_t* route_positions;
+    uint32_t* work_expert64;    /* may be NULL                                */
+    uint32_t* work_start64;
+    uint32_t* work_expert128;
+    uint32_t* work_start128;
+    void* route_ws;             /* b2_moe_route_workspace_size(rows, experts) */
+    size_t route_ws_bytes;
+} b2_prefill_work;
+
+/*
+ * Runs the non-GEMM path of all `num_layers` decoder layers plus the final
+ * add + LayerNorm on trie-node rows, in the order of
+ * PhiDecoderLayer::forward_carry (src/layer.cu:273-300) and
+ * PhiTinyMoEModel::generate (src/model.cu:119-150):
+ * embedding gather of node_token; per layer: LN1 (layer 0) or the previous
+ * layer's un-permute + carried add + LN1 (fused), RoPE at node_depth,
+ * attn += x + LN2, top-2 routing, SiLU(gate)*up; finally the last
+ * un-permute + carried add + final LN. final_x receives the final residual
+ * stream and final_out its LayerNorm ([rows, hidden] each).
+ *
+ * `events` (NULL for none) is an array of 2 * (5 * num_layers + 1)
+ * cudaEvent_t handles recorded on `stream` around each launch, pair i at
+ * [2i, 2i+1]: i = l < num_layers is layer l's LN1 step (plain LN for l = 0,
+ * the fused un-permute + add + LN otherwise), i = num_layers the final fused
+ * step, i = num_layers + 1 + 4l + s layer l's RoPE (s = 0), add + LN2 (1),
+ * routing (2) and SiLU (3). Kernel launches issued: B2_PREFILL_LAUNCHES(L).
+ */
+#define B2_PREFILL_LAUNCHES(num_layers) (2 + 6 * (num_layers))
+int b2_prefill_layers(const b2_prefill_shape* shape, const float* emb, size_t vocab,
+                      const uint32_t* node_token, const uint32_t* node_depth,
+                      const float* rope_cos, const float* rope_sin, size_t rope_rows,
+                      const b2_prefill_layer* layers, size_t num_layers,
+                      const float* final_gamma, const float* final_beta,
+                      const b2_prefill_work* work, float* final_x, float* final_out,
+                      void* const* events, b2_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

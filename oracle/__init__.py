@@ -274,3 +274,44 @@ def assert_bitexact(got, want, what=""):
         i = diff[0]
         raise AssertionError(f"{what}: {diff.size} elements differ; first at {i}: "
                              f"got {got.ravel()[i]!r} want {want.ravel()[i]!r}")
+
+
+# ---- layer pipeline ------------------------------------------------------------------------
+
+
+def prefill_layers(emb, node_token, node_depth, standins, ln1, ln2, final, layers, q_heads=16, kv_heads=4,
+                   head_dim=128, inter=448, eps=1e-5, theta=10000.0):
+    """The non-GEMM layer loop of PhiDecoderLayer::forward_carry
+    (src/layer.cu:273-300) and the final add + LayerNorm of
+    PhiTinyMoEModel::generate (src/model.cu:119-150) with the oracle ops, in
+    the reference's unfused order (k_moe_combine into x, then
+    k_add_layer_norm with the carry). `standins` is a list of dicts of host
+    arrays (q, k, attn, logits, gate_up, expert_out), layer l using
+    standins[l % len]; q, k and attn are updated in place as on the GPU.
+    Returns (final_x, final_out)."""
+    node_depth = u32(node_depth)
+    x = gather_rows(emb, node_token)
+    rows, h = x.shape
+    cos, sin = rope_table(int(node_depth.max()) + 1, head_dim, theta)
+    carry = None
+    routing = None
+    prev = None
+    for l in range(layers):
+        s = standins[l % len(standins)]
+        if l == 0:
+            normed = layer_norm(x, ln1[l][0], ln1[l][1], eps)
+        else:
+            x = moe_combine(prev["expert_out"], routing["routes"], routing["route_positions"], rows)
+            x, normed = add_layer_norm(x, carry, ln1[l][0], ln1[l][1], eps)
+        q, k = rope(s["q"], s["k"], node_depth, q_heads, kv_heads, head_dim, cos, sin)
+        s["q"][...] = q
+        s["k"][...] = k
+        attn, post = add_layer_norm(s["attn"], x, ln2[l][0], ln2[l][1], eps)
+        s["attn"][...] = attn
+        routing = route = moe_route(s["logits"])
+        act = silu_mul(s["gate_up"][:, :inter], s["gate_up"][:, inter:])
+        carry = s["attn"].copy()
+        prev = s
+        del normed, post, act, route
+    x = moe_combine(prev["expert_out"], routing["routes"], routing["route_positions"], rows)
+    return add_layer_norm(x, carry, final[0], final[1], eps)

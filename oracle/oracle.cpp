@@ -137,7 +137,8 @@ void orc_rope_table(std::size_t max_seq, std::size_t head_dim, float theta,
 
 // k_rope (src/tensor.cu:2180-2197), applied to q then k. nvcc fuses
 // `x0 * c - x1 * s` into fma(x0, c, -(x1 * s)) and `x1 * c + x0 * s` into
-// fma(x1, c, x0 * s).
+// fma(x0, s, x1 * c) -- the second product is the fused one there (pinned
+// against the reference kernel's own output, tests/golden/ref_kernels.npz).
 static void rope_one(float* x, const std::uint32_t* row_pos,
                      const float* cosine, const float* sine, std::size_t rows,
                      std::size_t heads, std::size_t head_dim) {
@@ -151,7 +152,7 @@ static void rope_one(float* x, const std::uint32_t* row_pos,
                 const float c = cosine[t + j], s = sine[t + j];
                 const float x0 = base[j], x1 = base[j + half];
                 base[j] = std::fma(x0, c, -(x1 * s));
-                base[j + half] = std::fma(x1, c, x0 * s);
+                base[j + half] = std::fma(x0, s, x1 * c);
             }
         }
     }

@@ -71,7 +71,13 @@ def gpu_kernels() -> dict:
     r = oracle.ref()
     dev = torch.device("cuda", 0)
     st = torch.cuda.current_stream().cuda_stream
-    d = lambda a: torch.from_numpy(np.ascontiguousarray(a.view(np.int32) if a.dtype == np.uint32 else a)).to(dev)  # noqa: E731
+    keep = []  # device copies stay alive until the end: a temporary's block could be reused before its kernel runs
+
+    def d(a):
+        t = torch.from_numpy(np.ascontiguousarray(a.view(np.int32) if a.dtype == np.uint32 else a)).to(dev)
+        keep.append(t)
+        return t
+
     host = lambda t: t.cpu().numpy()  # noqa: E731
 
     def run(rc):

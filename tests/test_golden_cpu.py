@@ -5,9 +5,10 @@ Fixtures (tests/golden/make_golden.py):
                       apply_rope, silu + mul, add_inplace);
   ref_kernels.npz  -- the reference's CUDA kernels, run on a B200 from the
                       reference's own source (oracle/_ref).
-Both must match the oracle bit for bit (the oracle follows the kernels'
-arithmetic, fused multiply-adds included; the host ops, built as the
-reference builds them, happen to agree with it exactly).
+The kernel fixtures must match the oracle bit for bit (the oracle follows
+the kernels' arithmetic, fused multiply-adds included). The host ops agree
+bit for bit too except apply_rope, whose host build fuses the other product
+of `x1 * c + x0 * s` than nvcc does in k_rope; it agrees within tolerance.
 """
 from pathlib import Path
 
@@ -43,8 +44,8 @@ def test_host_rope(host_ops):
     pos = np.concatenate([np.arange(n) for n in lens]).astype(np.uint32)
     c, s = oracle.rope_table(int(lens.max()), 128, 10000.0)
     q, k = oracle.rope(f["rope_q"], f["rope_k"], pos, 4, 1, 128, c, s)
-    oracle.assert_bitexact(q, f["rope_q_out"], "rope q")
-    oracle.assert_bitexact(k, f["rope_k_out"], "rope k")
+    oracle.assert_close(q, f["rope_q_out"], what="rope q")
+    oracle.assert_close(k, f["rope_k_out"], what="rope k")
 
 
 def test_host_silu_add(host_ops):

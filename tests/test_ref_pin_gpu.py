@@ -232,10 +232,10 @@ def test_ref_softmax_via_attention(ops, cuda, T):
     pos = np.arange(T, dtype=np.uint32)
     anc = np.tile(np.arange(T, dtype=np.uint32), (T, 1))
     qd, kd = to_dev(q.reshape(T, qh * hd), cuda), to_dev(eye, cuda)
+    pd, ad = to_dev(pos, cuda), to_dev(anc, cuda)
     out = torch.empty((T, qh * hd), device=cuda)
     _run(oracle.ref().ref_k_attention_tree(qd.data_ptr(), kd.data_ptr(), kd.data_ptr(), out.data_ptr(),
-                                           to_dev(pos, cuda).data_ptr(), to_dev(anc, cuda).data_ptr(), T, T, T,
-                                           qh, kh, hd, _stream()))
+                                           pd.data_ptr(), ad.data_ptr(), T, T, T, qh, kh, hd, _stream()))
     ref_p = to_host(out).reshape(T, qh, hd)[:, :, :T].transpose(1, 0, 2)  # [heads, query, key]
     scores = np.ascontiguousarray(q[:, :, :T].transpose(1, 0, 2))
     scale = np.float32(1.0) / np.sqrt(np.float32(128.0))  # 1.0f / sqrtf(128.0f), as the kernel forms it
