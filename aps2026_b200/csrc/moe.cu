@@ -7,19 +7,23 @@
 // k_moe_fill_stable (:1376-1418) runs 16 CTAs, each scanning ALL T tokens
 // for its expert -- 16x the routes traffic on 16 of 148 SMs.
 //
-// Here the same outputs come from two launches over 256-token tiles:
+// Here the same outputs come from two launches over 256-token tiles, with
+// no serial step and no waiting between CTAs:
 //   1. route_select: per token the quantized scores and the scan-order
-//      top-2 pick (same float operations and comparisons as k_moe_top2),
-//      per tile an expert histogram in shared memory. The last tile to
-//      finish (an atomic ticket, no waiting) scans the per-tile histograms
-//      for every expert (warp-parallel), writes counts / offsets and both
-//      work queues, and re-arms the ticket.
-//   2. route_scatter: per tile, warp ballots give each token's stable rank
-//      among the tile's tokens of the same expert; rank + tile prefix +
-//      expert offset is the position, written to assignment_rows and
-//      route_positions. Token order within an expert is ascending, which is
-//      exactly what k_moe_fill_stable produces.
-// The integer outputs are bit-identical to the reference's.
+//      top-2 pick (same float operations and comparisons as k_moe_top2);
+//      per tile an expert histogram (shared-memory atomics) written to the
+//      workspace.
+//   2. route_scatter: every CTA reads the whole histogram table from L2
+//      (128-bit loads, E padded to a power of two >= 4) and forms, per
+//      expert, the total and the count in tiles before its own -- so
+//      offsets and its tile base need no global scan pass; warp ballots then
+//      give each token's stable rank among the tile's tokens of the same
+//      expert, and rank + tile base + expert offset is the position written
+//      to assignment_rows and route_positions. CTA 0 writes counts/offsets;
+//      all CTAs together write the two work queues.
+// Token order within an expert is ascending, exactly what
+// k_moe_fill_stable produces; all integer outputs are bit-identical.
+#include "fastexp.cuh"
 #include "rowload.cuh"
 
 namespace b2 {
@@ -27,11 +31,19 @@ namespace {
 
 constexpr int kTile = 256;          // tokens per routing tile = threads per CTA
 constexpr int kMaxExperts = 32;
-constexpr std::size_t kWsHeader = 256;  // ticket word + padding
+
+// Histogram row stride: E rounded up to a power of two >= 4, so a tile's
+// counts are whole 16-byte vectors.
+inline unsigned padded_experts(std::size_t E) {
+    unsigned p = 4;
+    while (p < E) p <<= 1;
+    return p;
+}
 
 struct RouteArgs {
     const float* logits;
     std::size_t T, E;
+    unsigned EP;                 // padded_experts(E)
     float quantum, tie_eps;
     std::uint8_t* routes;
     std::uint32_t* counts;
@@ -42,8 +54,7 @@ struct RouteArgs {
     std::uint32_t* ws64;
     std::uint32_t* we128;
     std::uint32_t* ws128;
-    std::uint32_t* ticket;       // workspace word 0
-    std::uint32_t* tile_counts;  // [tiles][E], becomes per-expert exclusive prefix
+    std::uint32_t* tile_counts;  // [tiles][EP]
     std::size_t tiles;
 };
 
@@ -58,11 +69,8 @@ __device__ __forceinline__ float quantize(float s, float quantum) {
 __global__ void __launch_bounds__(kTile)
 route_select(RouteArgs a) {
     __shared__ unsigned int hist[kMaxExperts];
-    __shared__ unsigned int totals[kMaxExperts];
-    __shared__ unsigned int offs[kMaxExperts + 1], q64[kMaxExperts + 1], q128[kMaxExperts + 1];
-    __shared__ bool is_last;
     const unsigned E = static_cast<unsigned>(a.E);
-    if (threadIdx.x < E) hist[threadIdx.x] = 0;
+    if (threadIdx.x < kMaxExperts) hist[threadIdx.x] = 0;
     __syncthreads();
 
     const std::size_t t = static_cast<std::size_t>(blockIdx.x) * kTile + threadIdx.x;
@@ -109,86 +117,98 @@ route_select(RouteArgs a) {
         atomicAdd(&hist[second], 1u);
     }
     __syncthreads();
-    if (threadIdx.x < E) a.tile_counts[static_cast<std::size_t>(blockIdx.x) * E + threadIdx.x] = hist[threadIdx.x];
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (!is_last) return;
+    if (threadIdx.x < a.EP)
+        a.tile_counts[static_cast<std::size_t>(blockIdx.x) * a.EP + threadIdx.x] = hist[threadIdx.x];
+}
 
-    // ---- last tile: per-expert scan over tiles, counts, offsets, queues ----
-    __threadfence();
-    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (unsigned e = warp; e < E; e += kTile / 32) {
-        unsigned running = 0;
-        for (std::size_t base = 0; base < a.tiles; base += 32) {
-            const std::size_t tile = base + lane;
-            const unsigned c = tile < a.tiles ? __ldcg(a.tile_counts + tile * E + e) : 0u;
-            unsigned incl = c;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= static_cast<unsigned>(o)) incl += n;
-            }
-            if (tile < a.tiles) a.tile_counts[tile * E + e] = running + incl - c;
-            running += __shfl_sync(0xffffffffu, incl, 31);
-        }
-        if (lane == 0) totals[e] = running;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned off = 0, w64 = 0, w128 = 0;
-        for (unsigned e = 0; e < E; ++e) {
-            a.counts[e] = totals[e];
-            a.offsets[e] = off;
-            offs[e] = off;
-            q64[e] = w64;
-            q128[e] = w128;
-            off += totals[e];
-            w64 += (totals[e] + 63) / 64;
-            w128 += (totals[e] + 127) / 128;
-        }
-        a.offsets[E] = off;
-        q64[E] = w64;
-        q128[E] = w128;
-        *a.ticket = 0;  // re-armed for the next call
-    }
-    __syncthreads();
-    const std::size_t n64 = (2 * a.T + 63) / 64 + a.E, n128 = (2 * a.T + 127) / 128 + a.E;
-    // Queue entry i belongs to the expert whose chunk range holds it; entries
-    // past the last chunk are 0xFFFFFFFF (the reference memsets the expert
-    // queues to 0xff; the start queues get the same marker here).
-    for (std::size_t i = threadIdx.x; i < n64; i += kTile) {
-        std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
-        if (i < q64[E]) {
-            unsigned e = 0;
-            while (i >= q64[e + 1]) ++e;
-            ex = e;
-            st = offs[e] + static_cast<std::uint32_t>(i - q64[e]) * 64u;
-        }
-        if (a.we64) a.we64[i] = ex;
-        if (a.ws64) a.ws64[i] = st;
-    }
-    for (std::size_t i = threadIdx.x; i < n128; i += kTile) {
-        std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
-        if (i < q128[E]) {
-            unsigned e = 0;
-            while (i >= q128[e + 1]) ++e;
-            ex = e;
-            st = offs[e] + static_cast<std::uint32_t>(i - q128[e]) * 128u;
-        }
-        if (a.we128) a.we128[i] = ex;
-        if (a.ws128) a.ws128[i] = st;
-    }
+__device__ __forceinline__ uint4 add_u4(uint4 a, const uint4& b) {
+    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    return a;
+}
+
+__device__ __forceinline__ uint4 shfl_xor_u4(const uint4& v, int o) {
+    return make_uint4(__shfl_xor_sync(0xffffffffu, v.x, o), __shfl_xor_sync(0xffffffffu, v.y, o),
+                      __shfl_xor_sync(0xffffffffu, v.z, o), __shfl_xor_sync(0xffffffffu, v.w, o));
 }
 
 __global__ void __launch_bounds__(kTile)
 route_scatter(RouteArgs a) {
     constexpr int WARPS = kTile / 32;
+    __shared__ uint4 red_all[WARPS][kMaxExperts / 4], red_before[WARPS][kMaxExperts / 4];
+    __shared__ unsigned int base_s[kMaxExperts], offs_s[kMaxExperts + 1];
+    __shared__ unsigned int q64_s[kMaxExperts + 1], q128_s[kMaxExperts + 1];
     __shared__ unsigned int warp_cnt[WARPS][kMaxExperts];
     __shared__ unsigned int warp_base[WARPS][kMaxExperts];
     const unsigned E = static_cast<unsigned>(a.E);
     const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+    // ---- expert totals and this tile's base, from the histogram table ----
+    const unsigned ep4 = a.EP / 4;              // 16-byte vectors per tile
+    const unsigned sub = threadIdx.x % ep4, trow = threadIdx.x / ep4;
+    const unsigned per_pass = kTile / ep4;      // tiles covered per pass
+    const uint4* tc4 = reinterpret_cast<const uint4*>(a.tile_counts);
+    uint4 all = make_uint4(0, 0, 0, 0), before = make_uint4(0, 0, 0, 0);
+#pragma unroll 4
+    for (std::size_t tile = trow; tile < a.tiles; tile += per_pass) {
+        const uint4 v = __ldcg(tc4 + tile * ep4 + sub);
+        all = add_u4(all, v);
+        if (tile < blockIdx.x) before = add_u4(before, v);
+    }
+    for (int o = 16; o >= static_cast<int>(ep4); o >>= 1) {  // lanes of equal `sub`
+        all = add_u4(all, shfl_xor_u4(all, o));
+        before = add_u4(before, shfl_xor_u4(before, o));
+    }
+    if (lane < ep4) {
+        red_all[warp][lane] = all;
+        red_before[warp][lane] = before;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const unsigned e = lane;
+        unsigned tot = 0, bef = 0;
+        if (e < E) {
+            const unsigned* ra = reinterpret_cast<const unsigned*>(&red_all[0][0]);
+            const unsigned* rb = reinterpret_cast<const unsigned*>(&red_before[0][0]);
+            for (int w = 0; w < WARPS; ++w) {
+                tot += ra[w * (kMaxExperts) + e];
+                bef += rb[w * (kMaxExperts) + e];
+            }
+        }
+        // exclusive scans over experts: offsets and the two queue bases
+        unsigned incl = tot, c64 = (tot + 63) / 64, c128 = (tot + 127) / 128;
+        unsigned i64 = c64, i128 = c128;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
+            const unsigned n64 = __shfl_up_sync(0xffffffffu, i64, o);
+            const unsigned n128 = __shfl_up_sync(0xffffffffu, i128, o);
+            if (lane >= static_cast<unsigned>(o)) { incl += n; i64 += n64; i128 += n128; }
+        }
+        if (e < E) {
+            offs_s[e] = incl - tot;
+            q64_s[e] = i64 - c64;
+            q128_s[e] = i128 - c128;
+            base_s[e] = incl - tot + bef;
+        }
+        // lane 31's inclusive sums are the grand totals (lanes >= E add 0)
+        const unsigned all_rows = __shfl_sync(0xffffffffu, incl, 31);
+        const unsigned all64 = __shfl_sync(0xffffffffu, i64, 31);
+        const unsigned all128 = __shfl_sync(0xffffffffu, i128, 31);
+        if (lane == 0) {
+            offs_s[E] = all_rows;
+            q64_s[E] = all64;
+            q128_s[E] = all128;
+        }
+        if (blockIdx.x == 0) {
+            if (e < E) {
+                a.counts[e] = tot;
+                a.offsets[e] = incl - tot;
+            }
+            if (lane == 0) a.offsets[E] = all_rows;
+        }
+    }
+
+    // ---- stable ranks inside the tile ----
     const std::size_t t = static_cast<std::size_t>(blockIdx.x) * kTile + threadIdx.x;
     const bool valid = t < a.T;
     unsigned e0 = 0xFFu, e1 = 0xFFu;
@@ -206,8 +226,7 @@ route_scatter(RouteArgs a) {
     __syncthreads();
     if (threadIdx.x < E) {
         const unsigned e = threadIdx.x;
-        unsigned base = __ldg(a.offsets + e) +
-                        a.tile_counts[static_cast<std::size_t>(blockIdx.x) * E + e];
+        unsigned base = base_s[e];
         for (int w = 0; w < WARPS; ++w) {
             warp_base[w][e] = base;
             base += warp_cnt[w][e];
@@ -224,13 +243,45 @@ route_scatter(RouteArgs a) {
         a.assignment_rows[p1] = static_cast<std::uint32_t>(t);
         reinterpret_cast<uint2*>(a.route_positions)[t] = make_uint2(p0, p1);
     }
+
+    // ---- work queues: entry i belongs to the expert whose chunk range holds
+    // it; entries past the last chunk are 0xFFFFFFFF (the reference memsets
+    // the expert queues to 0xff; the start queues get the same marker) ----
+    const std::size_t n64 = (2 * a.T + 63) / 64 + a.E, n128 = (2 * a.T + 127) / 128 + a.E;
+    const std::size_t nq = n64 > n128 ? n64 : n128;
+    for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * kTile + threadIdx.x; i < nq;
+         i += static_cast<std::size_t>(gridDim.x) * kTile) {
+        if (i < n64) {
+            std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
+            if (i < q64_s[E]) {
+                unsigned e = 0;
+                while (i >= q64_s[e + 1]) ++e;
+                ex = e;
+                st = offs_s[e] + static_cast<std::uint32_t>(i - q64_s[e]) * 64u;
+            }
+            if (a.we64) a.we64[i] = ex;
+            if (a.ws64) a.ws64[i] = st;
+        }
+        if (i < n128) {
+            std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
+            if (i < q128_s[E]) {
+                unsigned e = 0;
+                while (i >= q128_s[e + 1]) ++e;
+                ex = e;
+                st = offs_s[e] + static_cast<std::uint32_t>(i - q128_s[e]) * 128u;
+            }
+            if (a.we128) a.we128[i] = ex;
+            if (a.ws128) a.ws128[i] = st;
+        }
+    }
 }
 
 // ---- gated SiLU -------------------------------------------------------------
 
-// g / (1 + (float)exp((double)-g)) * u, k_silu_mul (src/tensor.cu:2005-2008).
-__device__ __forceinline__ float silu_mul1(float g, float u) {
-    const float act = __fdiv_rn(g, __fadd_rn(1.0f, static_cast<float>(exp(static_cast<double>(-g)))));
+// g / (1 + (float)exp((double)-g)) * u, k_silu_mul (src/tensor.cu:2005-2008);
+// the exponential bit-identical through exp_ref (fastexp.cuh).
+__device__ __forceinline__ float silu_mul1(float g, float u, const double* tab) {
+    const float act = __fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g, tab)));
     return __fmul_rn(act, u);
 }
 
@@ -242,6 +293,9 @@ __global__ void __launch_bounds__(kSiluThreads)
 silu_mul_vec(const float* __restrict__ gate, std::size_t ldg, const float* __restrict__ up,
              std::size_t ldu, float* __restrict__ out, std::size_t ldo, std::size_t rows,
              std::size_t c4) {
+    __shared__ double tab[64];
+    load_exp2_table(tab);
+    __syncthreads();
     const unsigned lane = threadIdx.x & 31;
     const std::size_t warps = static_cast<std::size_t>(gridDim.x) * (kSiluThreads / 32);
     for (std::size_t r = static_cast<std::size_t>(blockIdx.x) * (kSiluThreads / 32) + (threadIdx.x >> 5);
@@ -263,8 +317,8 @@ silu_mul_vec(const float* __restrict__ gate, std::size_t ldg, const float* __res
             for (int k = 0; k < kSiluUnroll; ++k) {
                 const std::size_t j = j0 + 32 * k;
                 if (j < c4)
-                    st_plain(o4 + j, make_float4(silu_mul1(g[k].x, u[k].x), silu_mul1(g[k].y, u[k].y),
-                                                 silu_mul1(g[k].z, u[k].z), silu_mul1(g[k].w, u[k].w)));
+                    st_plain(o4 + j, make_float4(silu_mul1(g[k].x, u[k].x, tab), silu_mul1(g[k].y, u[k].y, tab),
+                                                 silu_mul1(g[k].z, u[k].z, tab), silu_mul1(g[k].w, u[k].w, tab)));
             }
         }
     }
@@ -274,12 +328,15 @@ __global__ void __launch_bounds__(kSiluThreads)
 silu_mul_scalar(const float* __restrict__ gate, std::size_t ldg, const float* __restrict__ up,
                 std::size_t ldu, float* __restrict__ out, std::size_t ldo, std::size_t rows,
                 std::size_t cols) {
+    __shared__ double tab[64];
+    load_exp2_table(tab);
+    __syncthreads();
     const unsigned lane = threadIdx.x & 31;
     const std::size_t warps = static_cast<std::size_t>(gridDim.x) * (kSiluThreads / 32);
     for (std::size_t r = static_cast<std::size_t>(blockIdx.x) * (kSiluThreads / 32) + (threadIdx.x >> 5);
          r < rows; r += warps)
         for (std::size_t j = lane; j < cols; j += 32)
-            out[r * ldo + j] = silu_mul1(__ldg(gate + r * ldg + j), __ldg(up + r * ldu + j));
+            out[r * ldo + j] = silu_mul1(__ldg(gate + r * ldg + j), __ldg(up + r * ldu + j), tab);
 }
 
 // ---- weighted un-permute ----------------------------------------------------
@@ -360,7 +417,7 @@ extern "C" {
 
 int b2_moe_route_workspace_size(size_t T, size_t E, size_t* bytes) {
     if (!bytes) return b2::invalid("b2_moe_route_workspace_size: null bytes");
-    *bytes = b2::kWsHeader + b2::route_tiles(T) * E * sizeof(uint32_t);
+    *bytes = b2::route_tiles(T) * b2::padded_experts(E) * sizeof(uint32_t);
     return B2_OK;
 }
 
@@ -387,8 +444,8 @@ int b2_moe_route(const float* logits, size_t T, size_t E, float quantum, float t
     a.routes = routes; a.counts = counts; a.offsets = offsets;
     a.assignment_rows = assignment_rows; a.route_positions = route_positions;
     a.we64 = work_expert64; a.ws64 = work_start64; a.we128 = work_expert128; a.ws128 = work_start128;
-    a.ticket = static_cast<uint32_t*>(workspace);
-    a.tile_counts = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + kWsHeader);
+    a.EP = padded_experts(E);
+    a.tile_counts = static_cast<uint32_t*>(workspace);
     a.tiles = route_tiles(T);
     if (a.tiles > 0x7FFFFFFFu) return invalid("b2_moe_route: too many tiles");
     cudaStream_t s = as_stream(stream);

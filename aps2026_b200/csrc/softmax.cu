@@ -9,14 +9,16 @@
 // One CTA per query row (grid-stride over heads * T rows). The row's
 // in-window chunk of scores is read with 128-bit loads straight into
 // registers -- chunks wholly outside [i + 1 - window, i] are never read --
-// scaled, reduced to the max, exponentiated in double and rounded to float
-// as the reference does, summed, divided, and the full row (zeros outside
+// scaled, reduced to the max, exponentiated as the reference does --
+// (float)exp((double)d), bit for bit, through the table-driven exp_ref of
+// fastexp.cuh -- summed, divided, and the full row (zeros outside
 // the window) written with 128-bit stores. Default: tree-order denominator.
 // B2_FLAG_EXACT_ORDER: the exponentials are staged in shared memory and one
 // thread sums them in ascending key order, as the reference does, making the
 // output bit-identical.
 // HBM bound: 4 * (window cells) read + 4 * T written per row.
 #include "common.cuh"
+#include "fastexp.cuh"
 
 namespace b2 {
 namespace {
@@ -32,16 +34,15 @@ struct SoftmaxArgs {
     float scale;
 };
 
-__device__ __forceinline__ float exp_ref(float x) {
-    return static_cast<float>(exp(static_cast<double>(x)));
-}
-
 template <int V, bool EXACT>
 __global__ void __launch_bounds__(kSmThreads)
 causal_softmax_reg(SoftmaxArgs a) {
     __shared__ float red[2][kSmWarps];
     __shared__ float denom_s;
+    __shared__ double tab[64];
     extern __shared__ __align__(16) float staged[];  // EXACT: T floats
+    load_exp2_table(tab);
+    __syncthreads();
     const std::size_t T4 = a.T / 4;
     for (std::size_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
         const std::size_t i = row % a.T;
@@ -74,7 +75,7 @@ causal_softmax_reg(SoftmaxArgs a) {
         for (int k = 0; k < V; ++k)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float ex = (valid >> (4 * k + e)) & 1u ? exp_ref(__fsub_rn(v[k][e], m)) : 0.0f;
+                const float ex = (valid >> (4 * k + e)) & 1u ? exp_ref(__fsub_rn(v[k][e], m), tab) : 0.0f;
                 v[k][e] = ex;
                 local_sum = __fadd_rn(local_sum, ex);
             }
@@ -118,7 +119,10 @@ __global__ void __launch_bounds__(kSmThreads)
 causal_softmax_smem(SoftmaxArgs a) {
     __shared__ float red[2][kSmWarps];
     __shared__ float denom_s;
+    __shared__ double tab[64];
     extern __shared__ __align__(16) float staged[];
+    load_exp2_table(tab);
+    __syncthreads();
     for (std::size_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
         const std::size_t i = row % a.T;
         const std::size_t begin = i + 1 > a.window ? i + 1 - a.window : 0;
@@ -133,7 +137,7 @@ causal_softmax_smem(SoftmaxArgs a) {
         const float m = block_max<kSmWarps>(local_max, red[0]);
         float local_sum = 0.0f;
         for (std::size_t j = begin + threadIdx.x; j <= i; j += kSmThreads) {
-            const float ex = exp_ref(__fsub_rn(staged[j], m));
+            const float ex = exp_ref(__fsub_rn(staged[j], m), tab);
             staged[j] = ex;
             local_sum = __fadd_rn(local_sum, ex);
         }

@@ -226,13 +226,13 @@ def queue_lengths(T: int, E: int) -> tuple[int, int]:
 
 
 class RouteWorkspace:
-    """Caller-owned routing scratch (zero-filled once; each call re-zeroes it)."""
+    """Caller-owned routing scratch (per-tile expert histograms)."""
 
     def __init__(self, T: int, E: int, device):
         n = C.c_size_t(0)
         _check(_lib.lib().b2_moe_route_workspace_size(T, E, C.addressof(n)), "workspace size")
         self.bytes = n.value
-        self.buf = torch.zeros(self.bytes, dtype=torch.uint8, device=device)
+        self.buf = torch.empty(max(self.bytes, 16), dtype=torch.uint8, device=device)
 
 
 def alloc_routing(T: int, E: int, device) -> MoeRouting:

@@ -1,0 +1,487 @@
+"""Benchmark of the non-GEMM Phi-tiny-MoE prefill path on B200.
+
+Workload: 64 prompts x 2048 tokens (ids uniform over
+the 32064-token vocabulary, seed 4), prefix-trie dedup, all 32 layers'
+non-GEMM ops (embedding gather, LayerNorms, RoPE, attn += x + LayerNorm,
+top-2 routing + permutation, SiLU(gate) * up, un-permute fused with the
+carried add + LayerNorm), final add + LayerNorm, expansion to token rows and
+-- on N > 1 GPUs -- one NCCL gather of the final hidden states
+[64 x 2048, 4096] to rank 0. Prompts are sharded across ranks (strong
+scaling: the 64-prompt batch is fixed). GEMM outputs are seeded N(0,1)
+stand-ins of the config.h shapes, a pool of them reused round-robin across
+the 32 layers (each set far larger than L2).
+
+One "step" = that whole pass. `value` is tokens/s over all ranks with the
+inputs resident in HBM; `e2e` is the same step through the public API from
+host token ids (host trie build, H2D of the index arrays, D2H of the last-
+token hidden states). `--impl reference` times the reference's own host
+implementation of the path (oracle/_ref) on a bounded sample instead.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "non-GEMM prefill tokens/s (64x2048 prompts, 32 layers; layer-op HBM GB/s in roofline)"
+# DRAM bytes per launch of the dominant kernel, from the ncu capture in
+# profiles/fused_combine_add_ln.md (per node row; scaled by rows).
+TRAFFIC_BYTES_PER_ROW = None
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--exact", action="store_true", help="B2_FLAG_EXACT_ORDER reductions")
+    p.add_argument("--prompts", type=int, default=64)
+    p.add_argument("--length", type=int, default=2048)
+    p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--pool", type=int, default=0, help="stand-in sets (0 = fit to memory)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---- clocks ----------------------------------------------------------------------------
+
+
+class ClockSampler:
+    """Samples this GPU's SM clock and clock-event reasons with NVML every
+    100 ms while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._handle = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device_index)
+            self._nvml = pynvml
+            uuid = str(props.uuid)
+            try:
+                self._handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+                self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # no NVML: report it, never guess
+            self.error = f"{type(exc).__name__}: {exc}"
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self._handle, n.NVML_CLOCK_SM))
+                mask = n.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._handle is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if self._handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---- distributed plumbing ----------------------------------------------------------------
+
+
+def dist_setup(n_gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torch.distributed.run")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def shard(prompts, rank: int, world: int) -> list[int]:
+    from aps2026_b200.shard import shard_prompts
+
+    return shard_prompts(prompts, world)[rank]
+
+
+# ---- our arm --------------------------------------------------------------------------------
+
+
+def run_ours(args):
+    import torch
+
+    from aps2026_b200 import ops, prefill
+    from aps2026_b200.prefill import Batch, Pipeline, StageTimer, StandIns, Weights
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+    prompts = prefill.prompts_config5(batch=args.prompts, length=args.length)
+    mine = shard(prompts, rank, world)
+    my_prompts = [prompts[i] for i in mine]
+    tokens_total = sum(len(p) for p in prompts)
+
+    weights = Weights.make(dev, seed=4, layers=args.layers)
+    batch = Batch.build(my_prompts, dev)
+    R = batch.rows
+    pipe = Pipeline(batch, weights, dev, exact=args.exact)
+    free, _ = torch.cuda.mem_get_info(dev)
+    set_bytes = prefill.standin_bytes(R)
+    gather_bytes = (tokens_total if rank == 0 else 0) * prefill.HIDDEN * 4 + batch.tokens * prefill.HIDDEN * 4
+    pool = args.pool or int(max(1, min(args.layers, 8 if world == 1 else 32,
+                                       (free * 0.75 - gather_bytes) // set_bytes)))
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    t_gen = time.perf_counter()
+    standins = [StandIns.make(R, dev, gen) for _ in range(pool)]
+    torch.cuda.synchronize()
+    t_gen = time.perf_counter() - t_gen
+    pipe.bind_layers(standins, args.layers)
+
+    # the step's collective: final hidden states of every token row to rank 0
+    send = torch.empty((batch.tokens, prefill.HIDDEN), device=dev)
+    shard_tokens = max(sum(len(prompts[i]) for i in shard(prompts, r, world)) for r in range(world))
+    if world > 1 and batch.tokens != shard_tokens:
+        raise SystemExit("unequal shards: the gather below expects equal token counts per rank")
+    recv = [torch.empty_like(send) for _ in range(world)] if (world > 1 and rank == 0) else None
+    last = torch.empty((len(my_prompts), prefill.HIDDEN), device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(timer=None):
+        pipe.run(timer=timer)
+        pipe.expand_to_tokens(send)
+        if world > 1:
+            dist.gather(send, recv, dst=0)
+
+    launches_per_step = prefill.launches_per_run(args.layers) + 1
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    timers = [StageTimer(args.layers) for _ in range(args.steps)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        ev[0].record(stream)
+        for k in range(args.steps):
+            step(timers[k])
+            ev[k + 1].record(stream)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+    ms = ev[0].elapsed_time(ev[args.steps])
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+
+    # per-kernel durations inside the timed region (this rank)
+    dur = {}
+    for tm in timers:
+        for k, v in tm.durations().items():
+            dur.setdefault(k, []).extend(v)
+    bpr = prefill.bytes_per_row(args.layers)
+    kern = {}
+    for k, v in dur.items():
+        per_launch_ms = statistics.mean(v)
+        total_ms = sum(v) / args.steps
+        nbytes = bpr[k if k in bpr else "ln0"] * R
+        kern[k] = dict(launches_per_step=len(v) // args.steps, ms_per_step=round(total_ms, 4),
+                       us_per_launch=round(per_launch_ms * 1e3, 2),
+                       gbs=round(nbytes / (per_launch_ms * 1e-3) / 1e9, 1))
+    dominant = max(kern, key=lambda k: kern[k]["ms_per_step"])
+
+    # e2e: host ids -> trie -> H2D -> layers -> gather -> D2H of last-token rows
+    ids_pinned = [torch.from_numpy(p).pin_memory() for p in my_prompts]
+    host_last = torch.empty((len(my_prompts), prefill.HIDDEN), pin_memory=True)
+
+    def e2e_step():
+        ids = [t.numpy() for t in ids_pinned]
+        b = Batch.build(ids, dev, pinned=True)
+        pipe.batch = b
+        step()
+        pipe.last_token_rows(last)
+        if rank == 0:
+            host_last.copy_(last, non_blocking=True)
+        return b
+
+    e2e_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for _ in range(1):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e2e_steps = max(1, min(args.steps, 3))
+    e2e_ev[0].record(stream)
+    for _ in range(e2e_steps):
+        b = e2e_step()
+    e2e_ev[1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e2e_ev[0].elapsed_time(e2e_ev[1]) / e2e_steps
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(int(x.numel()) * 4 for x in (b.node_token, b.node_depth, b.token_node, b.last_rows))
+    d2h = host_last.numel() * 4 if rank == 0 else 0
+
+    clk = clocks.summary()
+    if dist:
+        allclk = [None] * world
+        dist.all_gather_object(allclk, clk)
+        kern_all = [None] * world
+        dist.all_gather_object(kern_all, kern)
+    else:
+        allclk = [clk]
+
+    result = None
+    if rank == 0:
+        peak, peak_kind = peaks()
+        d = kern[dominant]
+        achieved = d["gbs"]
+        traffic = (TRAFFIC_BYTES_PER_ROW * R) if TRAFFIC_BYTES_PER_ROW else None
+        reasons = sorted(set(r for c in allclk for r in c.get("reasons", [])))
+        mhz = [c["sm_mhz"] for c in allclk if c.get("sm_mhz")]
+        tok_s = tokens_total / (ms_per_step / 1e3)
+        result = {
+            "metric": METRIC,
+            "value": round(tok_s, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded token ids; GEMM outputs are seeded N(0,1) stand-ins)",
+            "config": {"workload": f"config 5: {args.prompts} prompts x {args.length} tokens, {args.layers} layers, "
+                                   "non-GEMM path, final hidden states gathered to rank 0",
+                       "prompts": args.prompts, "tokens_per_prompt": args.length, "layers": args.layers,
+                       "node_rows_per_rank": R, "standin_pool": pool, "exact_order": args.exact,
+                       "l2": "inputs larger than L2 (every kernel streams >= 100 MB per launch)",
+                       "parallelism": f"prompt shards x{world}" + (", NCCL gather to rank 0" if world > 1 else "")},
+            "hbm_gbs_algorithmic": round(bpr["total"] * R * world / (ms_per_step / 1e3) / 1e9, 1),
+            "roofline": {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 3), "peak_kind": peak_kind,
+                         "traffic": traffic},
+            "kernels": kern,
+            "clocks": {"sm_mhz": statistics.median(mhz) if mhz else None,
+                       "sm_max_mhz": allclk[0].get("sm_max_mhz"), "reasons": reasons},
+            "e2e": {"value": round(tokens_total / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps * world,
+            "standin_gen_s": round(t_gen, 2),
+        }
+    if dist:
+        recv = None
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+# ---- CPU baseline / reference arm ---------------------------------------------------------
+
+
+def cpu_sample_inputs(rows: int, seed: int = 7):
+    """Host stand-ins for a bounded CPU sample of the same workload."""
+    from aps2026_b200 import prefill as P
+
+    g = np.random.default_rng(seed)
+    n = lambda *s: g.standard_normal(s, dtype=np.float32)  # noqa: E731
+    # the sample gathers `rows` embedding rows; a table of `rows` rows suffices
+    prompts = [g.integers(0, rows, 2048).astype(np.int32) for _ in range(rows // 2048)]
+    emb = (n(rows, P.HIDDEN) * 0.02).astype(np.float32)
+    s = dict(q=n(rows, P.Q_HEADS * P.HEAD_DIM), k=n(rows, P.KV_HEADS * P.HEAD_DIM), attn=n(rows, P.HIDDEN),
+             logits=n(rows, P.EXPERTS), gate_up=n(2 * rows, 2 * P.INTER), expert_out=n(2 * rows, P.HIDDEN))
+    ln = [(1 + 0.1 * n(P.HIDDEN), 0.1 * n(P.HIDDEN)) for _ in range(2)]
+    return prompts, emb, s, ln
+
+
+def cpu_baseline_port(rows: int = 8192, budget_s: float = 10.0) -> dict:
+    """The CPU oracle (a restatement of the reference kernels, OpenMP on all
+    host threads) over a bounded sample: one-layer passes of the pipeline
+    (gather, layer, final add + LN) on `rows` rows, repeated until about
+    `budget_s` seconds; tokens/s scaled to the 32-layer path."""
+    import oracle
+
+    prompts, emb, s, ln = cpu_sample_inputs(rows)
+    trie = oracle.prefix_trie(prompts, with_ancestors=False)
+    passes, t = 0, 0.0
+    while t < budget_s and passes < 32:
+        t0 = time.perf_counter()
+        oracle.prefill_layers(emb, trie["node_token"], trie["node_depth"], [s], [ln[0]], [ln[1]], ln[0], 1)
+        t += time.perf_counter() - t0
+        passes += 1
+    return {"value": round(rows * passes / 32 / t, 1), "unit": "tokens/s", "cores": oracle.num_threads(),
+            "kind": "port",
+            "sample": f"oracle pipeline, {passes} one-layer passes over {rows} rows (gather + layer + final LN), "
+                      f"{t:.1f} s, scaled to 32 layers"}
+
+
+def reference_layer(rows: int, s, ln, emb, node_token, node_depth, lens) -> float:
+    """One decoder layer's non-GEMM path on the CPU through the reference's
+    own host ops (oracle/_ref: tensor_ops::layer_norm, apply_rope, add_inplace,
+    silu + mul, as PhiDecoderLayer::forward's CPU branch calls them,
+    src/layer.cu:302-326); the top-2 routing and the expert un-permute, whose
+    reference CPU code is private to PhiMoE (src/layer.cu:69-92, :123-147),
+    run through the oracle's restatement. Returns seconds of op time."""
+    import ctypes as C
+
+    import oracle
+
+    r = oracle.ref()
+    sec = C.c_double()
+    total = 0.0
+    from aps2026_b200 import prefill as P
+
+    h = P.HIDDEN
+    t0 = time.perf_counter()
+    x = oracle.gather_rows(emb, node_token)
+    total += time.perf_counter() - t0
+    normed = np.empty_like(x)
+    r.ref_cpu_layer_norm(x.ctypes.data, ln[0][0].ctypes.data, ln[0][1].ctypes.data, normed.ctypes.data, rows, h,
+                         1e-5, C.addressof(sec))
+    total += sec.value
+    lens_arr = np.asarray(lens, dtype=np.uint64)
+    r.ref_cpu_apply_rope(s["q"].ctypes.data, s["k"].ctypes.data, lens_arr.ctypes.data, len(lens), P.Q_HEADS,
+                         P.KV_HEADS, P.HEAD_DIM, 1e4, C.addressof(sec))
+    total += sec.value
+    attn = s["attn"]
+    r.ref_cpu_add_inplace(attn.ctypes.data, x.ctypes.data, attn.size, C.addressof(sec))
+    total += sec.value
+    post = np.empty_like(attn)
+    r.ref_cpu_layer_norm(attn.ctypes.data, ln[1][0].ctypes.data, ln[1][1].ctypes.data, post.ctypes.data, rows, h,
+                         1e-5, C.addressof(sec))
+    total += sec.value
+    t0 = time.perf_counter()
+    route = oracle.moe_route(s["logits"])
+    total += time.perf_counter() - t0
+    gate = np.ascontiguousarray(s["gate_up"][:, :P.INTER])
+    up = np.ascontiguousarray(s["gate_up"][:, P.INTER:])
+    act = np.empty_like(gate)
+    r.ref_cpu_silu_mul(gate.ctypes.data, up.ctypes.data, act.ctypes.data, gate.size, C.addressof(sec))
+    total += sec.value
+    t0 = time.perf_counter()
+    ff = oracle.moe_combine(s["expert_out"], route["routes"], route["route_positions"], rows)
+    total += time.perf_counter() - t0
+    r.ref_cpu_add_inplace(ff.ctypes.data, attn.ctypes.data, ff.size, C.addressof(sec))
+    total += sec.value
+    return total
+
+
+def run_reference(args):
+    import oracle
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    if not oracle.ref_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libref.so (the reference built from its source) "
+                                                    "is missing; build it with `make -C oracle` where the "
+                                                    "reference tree exists"}
+    rows = 2048
+    prompts, emb, s, ln = cpu_sample_inputs(rows, seed=8)
+    trie = oracle.prefix_trie(prompts, with_ancestors=False)
+    lens = [len(p) for p in prompts]
+    base = {k: v.copy() for k, v in s.items()}
+    for _ in range(args.warmup):
+        reference_layer(rows, {k: v.copy() for k, v in base.items()}, ln, emb, trie["node_token"],
+                        trie["node_depth"], lens)
+    secs = []
+    for _ in range(args.steps):
+        secs.append(reference_layer(rows, {k: v.copy() for k, v in base.items()}, ln, emb, trie["node_token"],
+                                    trie["node_depth"], lens))
+    t_layer = statistics.mean(secs)
+    tokens_total = args.prompts * args.length
+    ms_per_step = t_layer * args.layers * (tokens_total / rows) * 1e3
+    value = tokens_total / (ms_per_step / 1e3)
+    sample = (f"reference host ops (oracle/_ref) for LN / RoPE / add / SiLU*mul, oracle port for routing and "
+              f"un-permute; one layer on {rows} rows ({t_layer:.3f} s), scaled to {args.layers} layers x "
+              f"{tokens_total} tokens")
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": f"config 5: {args.prompts} prompts x {args.length} tokens, "
+                                                        f"{args.layers} layers, non-GEMM path (CPU sample)"},
+            "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": oracle.num_threads(),
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        res = run_reference(args)
+        if res is not None:
+            print(json.dumps(res))
+        return
+    res = run_ours(args)
+    if res is not None:
+        if args.gpus == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline_port()
+        print(json.dumps(res))
+
+
+if __name__ == "__main__":
+    main()

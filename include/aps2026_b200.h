@@ -188,8 +188,9 @@ int b2_moe_route_workspace_size(size_t T, size_t E, size_t* bytes);
  *      any queue pointer may be NULL to skip it)
  * Scores are quantized to `quantum` (reference 1e-3) and picked by an
  * ascending scan that only replaces on > best + tie_eps (reference 2e-2).
- * The workspace (b2_moe_route_workspace_size bytes) must be zero-filled
- * before its first use; each call leaves it zero-filled again.
+ * The workspace (b2_moe_route_workspace_size bytes, 16-byte aligned) holds
+ * per-tile expert histograms between the two launches; it needs no
+ * initialisation. Calls that overlap on the GPU must not share it.
  */
 int b2_moe_route(const float* logits, size_t T, size_t E, float quantum,
                  float tie_eps, uint8_t* routes, uint32_t* counts,
@@ -252,6 +253,19 @@ int b2_prefix_trie_build(const int32_t* ids, const uint32_t* seq_lens,
                          uint32_t* token_node, uint32_t* node_token,
                          uint32_t* node_depth, uint32_t* node_anc,
                          size_t anc_stride, size_t* nodes_out);
+
+/* ---- diagnostics --------------------------------------------------------------- */
+
+/*
+ * Checks the kernels' fast (float)exp((double)x) -- a table-driven double
+ * evaluation that defers to exp(double) near float rounding midpoints --
+ * against exp(double) itself for every float whose bit pattern lies in
+ * [lo_bits, hi_bits). Synchronous; allocates a 24-byte counter block (a
+ * diagnostic, not a hot-path call). *mismatches must come back 0;
+ * *slow_path counts arguments that took the exp(double) path.
+ */
+int b2_selfcheck_exp(uint32_t lo_bits, uint32_t hi_bits, uint64_t* checked,
+                     uint64_t* mismatches, uint64_t* slow_path);
 
 /* ---- non-GEMM layer pipeline ------------------------------------------------ */
 

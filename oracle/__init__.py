@@ -90,10 +90,10 @@ def ref() -> C.CDLL:
             "ref_k_add": [_vp, _vp, _sz, _vp],
             "ref_k_attention_tree": [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _vp],
             "ref_sliding_window": [],
-            "ref_cpu_layer_norm": [_vp, _vp, _vp, _vp, _sz, _sz, _f32],
-            "ref_cpu_apply_rope": [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _f32],
-            "ref_cpu_silu_mul": [_vp, _vp, _vp, _sz],
-            "ref_cpu_add_inplace": [_vp, _vp, _sz],
+            "ref_cpu_layer_norm": [_vp, _vp, _vp, _vp, _sz, _sz, _f32, _vp],
+            "ref_cpu_apply_rope": [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _f32, _vp],
+            "ref_cpu_silu_mul": [_vp, _vp, _vp, _sz, _vp],
+            "ref_cpu_add_inplace": [_vp, _vp, _sz, _vp],
         }
         for name, args in sig.items():
             fn = getattr(h, name)

@@ -17,6 +17,7 @@
 
 #include "tensor.cu"
 
+#include <chrono>
 #include <cstdint>
 #include <vector>
 
@@ -43,6 +44,16 @@ Tensor host_output(std::vector<std::size_t> shape) {
 void copy_out(const Tensor& t, float* dst) {
     const float* s = t.data();
     std::copy(s, s + t.size(), dst);
+}
+
+// Times `op` alone (not the copies into and out of the reference Tensors);
+// stores seconds into *seconds when it is not null.
+template <typename F>
+void timed(double* seconds, F&& op) {
+    const auto t0 = std::chrono::steady_clock::now();
+    op();
+    const auto t1 = std::chrono::steady_clock::now();
+    if (seconds) *seconds = std::chrono::duration<double>(t1 - t0).count();
 }
 }  // namespace
 
@@ -152,12 +163,14 @@ int ref_k_attention_tree(const float* q, const float* k, const float* v,
 int ref_sliding_window(void) { return static_cast<int>(apss26::SLIDING_WINDOW); }
 
 // ---- host ops of the reference (host pointers) -----------------------------
+// Each takes an optional `seconds` out-parameter: the time of the reference
+// op itself, without the copies through its Tensor class.
 
 int ref_cpu_layer_norm(const float* x, const float* w, const float* b, float* y,
-                       std::size_t rows, std::size_t h, float eps) {
+                       std::size_t rows, std::size_t h, float eps, double* seconds) {
     Tensor tx = host_tensor(x, {rows, h}), tw = host_tensor(w, {h}),
            tb = host_tensor(b, {h}), ty = host_output({rows, h});
-    tensor_ops::layer_norm(tx, tw, tb, eps, ty);
+    timed(seconds, [&] { tensor_ops::layer_norm(tx, tw, tb, eps, ty); });
     copy_out(ty, y);
     return 0;
 }
@@ -165,30 +178,34 @@ int ref_cpu_layer_norm(const float* x, const float* w, const float* b, float* y,
 // apply_rope over packed segments (src/tensor.cu:343-367); q/k in place.
 int ref_cpu_apply_rope(float* q, float* k, const std::size_t* seq_lens,
                        std::size_t segments, std::size_t q_heads,
-                       std::size_t kv_heads, std::size_t head_dim, float theta) {
+                       std::size_t kv_heads, std::size_t head_dim, float theta,
+                       double* seconds) {
     std::vector<std::size_t> lens(seq_lens, seq_lens + segments);
     std::size_t rows = 0;
     for (std::size_t l : lens) rows += l;
     Tensor tq = host_tensor(q, {rows, q_heads * head_dim});
     Tensor tk = host_tensor(k, {rows, kv_heads * head_dim});
-    tensor_ops::apply_rope(tq, tk, lens, q_heads, kv_heads, head_dim, theta);
+    timed(seconds, [&] { tensor_ops::apply_rope(tq, tk, lens, q_heads, kv_heads, head_dim, theta); });
     copy_out(tq, q);
     copy_out(tk, k);
     return 0;
 }
 
 // silu then mul, as PhiMLP::forward does on the CPU (src/layer.cu:60-61).
-int ref_cpu_silu_mul(const float* gate, const float* up, float* out, std::size_t n) {
+int ref_cpu_silu_mul(const float* gate, const float* up, float* out, std::size_t n,
+                     double* seconds) {
     Tensor tg = host_tensor(gate, {n}), tu = host_tensor(up, {n}), act = host_output({n});
-    tensor_ops::silu(tg, act);
-    tensor_ops::mul(act, tu, act);
+    timed(seconds, [&] {
+        tensor_ops::silu(tg, act);
+        tensor_ops::mul(act, tu, act);
+    });
     copy_out(act, out);
     return 0;
 }
 
-int ref_cpu_add_inplace(float* a, const float* b, std::size_t n) {
+int ref_cpu_add_inplace(float* a, const float* b, std::size_t n, double* seconds) {
     Tensor ta = host_tensor(a, {n}), tb = host_tensor(b, {n});
-    tensor_ops::add_inplace(ta, tb);
+    timed(seconds, [&] { tensor_ops::add_inplace(ta, tb); });
     copy_out(ta, a);
     return 0;
 }

@@ -43,24 +43,24 @@ def host_ops() -> dict:
     rows, h = 16, 4096
     x, w, b = _n(g, (rows, h)), _n(g, h, 1.0, 0.1), _n(g, h, 0.0, 0.1)
     y = np.empty_like(x)
-    r.ref_cpu_layer_norm(x.ctypes.data, w.ctypes.data, b.ctypes.data, y.ctypes.data, rows, h, 1e-5)
+    r.ref_cpu_layer_norm(x.ctypes.data, w.ctypes.data, b.ctypes.data, y.ctypes.data, rows, h, 1e-5, None)
     out.update(ln_x=x, ln_w=w, ln_b=b, ln_y=y)
 
     lens = np.array([9, 4], dtype=np.uint64)
     qh, kh, hd = 4, 1, 128
     q, k = _n(g, (13, qh * hd)), _n(g, (13, kh * hd))
     rq, rk = q.copy(), k.copy()
-    r.ref_cpu_apply_rope(rq.ctypes.data, rk.ctypes.data, lens.ctypes.data, 2, qh, kh, hd, 10000.0)
+    r.ref_cpu_apply_rope(rq.ctypes.data, rk.ctypes.data, lens.ctypes.data, 2, qh, kh, hd, 10000.0, None)
     out.update(rope_q=q, rope_k=k, rope_lens=lens.astype(np.uint32), rope_q_out=rq, rope_k_out=rk)
 
     gate, up = _n(g, 3000, std=4.0), _n(g, 3000)
     act = np.empty_like(gate)
-    r.ref_cpu_silu_mul(gate.ctypes.data, up.ctypes.data, act.ctypes.data, gate.size)
+    r.ref_cpu_silu_mul(gate.ctypes.data, up.ctypes.data, act.ctypes.data, gate.size, None)
     out.update(silu_gate=gate, silu_up=up, silu_out=act)
 
     a, bb = _n(g, 3000), _n(g, 3000)
     s = a.copy()
-    r.ref_cpu_add_inplace(s.ctypes.data, bb.ctypes.data, a.size)
+    r.ref_cpu_add_inplace(s.ctypes.data, bb.ctypes.data, a.size, None)
     out.update(add_a=a, add_b=bb, add_out=s)
     return out
 

@@ -46,7 +46,9 @@ def test_null_pointer_arguments_are_rejected_before_any_device_work():
 def test_route_workspace_size():
     n = C.c_size_t(0)
     assert _lib.lib().b2_moe_route_workspace_size(8192, 16, C.addressof(n)) == 0
-    assert n.value == 256 + 32 * 16 * 4
+    assert n.value == 32 * 16 * 4
+    assert _lib.lib().b2_moe_route_workspace_size(1000, 13, C.addressof(n)) == 0
+    assert n.value == 4 * 16 * 4  # experts padded to a power of two
 
 
 @pytest.mark.parametrize("max_seq,head_dim,theta", [(4096, 128, 10000.0), (17, 64, 500000.0), (3, 2, 10.0)])

@@ -136,7 +136,8 @@ def test_ref_rope_cpu_twin_agrees():
     rows, qh, kh, hd = 10, 4, 1, 128
     q, k = normal(g, (rows, qh * hd)), normal(g, (rows, kh * hd))
     rq, rk = q.copy(), k.copy()
-    oracle.ref().ref_cpu_apply_rope(rq.ctypes.data, rk.ctypes.data, lens.ctypes.data, 2, qh, kh, hd, 10000.0)
+    oracle.ref().ref_cpu_apply_rope(rq.ctypes.data, rk.ctypes.data, lens.ctypes.data, 2, qh, kh, hd, 10000.0,
+                                    None)
     pos = np.concatenate([np.arange(7), np.arange(3)]).astype(np.uint32)
     c, s = oracle.rope_table(7, hd, 10000.0)
     wq, wk = oracle.rope(q, k, pos, qh, kh, hd, c, s)
@@ -195,7 +196,7 @@ def test_ref_silu_combine_add(ops, cuda):
     oracle.assert_bitexact(to_host(act), to_host(ref_act), "b2 vs ref silu")
     # ... and the reference's host silu + mul agrees bit for bit too
     host = np.empty_like(gate)
-    oracle.ref().ref_cpu_silu_mul(gate.ctypes.data, up.ctypes.data, host.ctypes.data, gate.size)
+    oracle.ref().ref_cpu_silu_mul(gate.ctypes.data, up.ctypes.data, host.ctypes.data, gate.size, None)
     oracle.assert_bitexact(host, to_host(ref_act), "ref host vs ref kernel silu")
 
     r = oracle.moe_route(normal(g, (T, 16)))

@@ -1,0 +1,37 @@
+"""The reference-side C++ binding (aps2026_b200/shim/tensor_ops_b2.cu)
+compiles against the reference's own include/tensor.h and config.h and
+defines exactly the tensor_ops functions it replaces, with the reference's
+signatures (checked through the mangled symbol names)."""
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+REF_INCLUDE = Path("/root/reference/include")
+
+EXPECTED = {
+    "tensor_ops::add_inplace_gpu(Tensor&, Tensor const&)",
+    "tensor_ops::silu_mul_gpu(Tensor const&, Tensor const&, Tensor&)",
+    "tensor_ops::layer_norm_gpu(Tensor const&, Tensor const&, Tensor const&, float, Tensor&)",
+    "tensor_ops::add_layer_norm_gpu(Tensor&, Tensor const&, Tensor const&, Tensor const&, float, Tensor&)",
+    "tensor_ops::apply_rope_gpu(Tensor&, Tensor&, std::vector<unsigned long, std::allocator<unsigned long> > const&, "
+    "unsigned long, unsigned long, unsigned long, float)",
+    "tensor_ops::apply_rope_tree_gpu(Tensor&, Tensor&, unsigned int const*, unsigned long, unsigned long, "
+    "unsigned long, unsigned long, unsigned long, float)",
+    "tensor_ops::gather_rows_gpu(Tensor const&, std::vector<unsigned long, std::allocator<unsigned long> > const&, "
+    "Tensor&)",
+    "tensor_ops::gather_rows_gpu(Tensor const&, tensor_ops::RowIndexBuffer const&, Tensor&)",
+}
+
+
+@pytest.mark.skipif(not (REF_INCLUDE / "tensor.h").exists(), reason="reference headers not present")
+def test_shim_compiles_against_reference_headers(tmp_path):
+    obj = tmp_path / "shim.o"
+    subprocess.run(["/usr/local/cuda/bin/nvcc", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-c",
+                    str(ROOT / "aps2026_b200/shim/tensor_ops_b2.cu"), f"-I{REF_INCLUDE}", f"-I{ROOT / 'include'}",
+                    "-o", str(obj)], check=True, capture_output=True)
+    nm = subprocess.run(["nm", "-C", "--defined-only", str(obj)], capture_output=True, text=True, check=True).stdout
+    defined = {line.split(" T ", 1)[1] for line in nm.splitlines() if " T tensor_ops::" in line
+               and "(anonymous namespace)" not in line}
+    assert defined == EXPECTED
