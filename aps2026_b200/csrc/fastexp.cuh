@@ -37,19 +37,21 @@ __device__ __forceinline__ float exp_ref_slow(float x) {
     return static_cast<float>(exp(static_cast<double>(x)));
 }
 
-// Returns (float)exp((double)x); `tab` is the shared table. `slow`, when
-// given, is set when the call took the exp(double) path.
+// Fast path of (float)exp((double)x), without branches so that a thread's
+// independent exponentials interleave. Sets *slow when the result must come
+// from exp_ref_slow instead: |x| > 80 (the float result may overflow or be
+// subnormal) or NaN, or y within the error bound of a float rounding
+// midpoint. The returned value is meaningless when *slow is set.
 //
 // Conversions are kept off the quarter-rate conversion pipe: n comes from
 // the low word of x * 64/ln2 + 1.5 * 2^52 (round to nearest integer by the
 // addition itself), and the final rounding of y to float is done on its bit
-// pattern (the near-midpoint case has already been excluded, so rounding
-// is "round half up" on the 29 dropped bits, and the carry runs into the
-// exponent field exactly as the next float up).
-__device__ __forceinline__ float exp_ref(float x, const double* tab, bool* slow = nullptr) {
-    if (slow) *slow = true;
-    if (!(fabsf(x) <= 80.0f)) return exp_ref_slow(x);  // also NaN
-    const double xd = static_cast<double>(x);
+// pattern (the near-midpoint case being excluded, rounding is "round half
+// up" on the 29 dropped bits, and the carry runs into the exponent field
+// exactly as the next float up).
+__device__ __forceinline__ float exp_ref_fast(float x, const double* tab, bool* slow) {
+    const bool out_of_range = !(fabsf(x) <= 80.0f);     // also NaN
+    const double xd = static_cast<double>(out_of_range ? 0.0f : x);
     const double shifter = 6755399441055744.0;          // 1.5 * 2^52
     const double tn = fma(xd, 92.332482616893656877, shifter);  // x * 64 / ln2, rounded to an integer
     const int n = __double2loint(tn);                   // that integer (|n| < 2^13)
@@ -66,13 +68,21 @@ __device__ __forceinline__ float exp_ref(float x, const double* tab, bool* slow 
     const unsigned lo = static_cast<unsigned>(__double2loint(y));
     const unsigned hi = static_cast<unsigned>(__double2hiint(y));
     const int low29 = static_cast<int>(lo & 0x1FFFFFFFu);
-    if (abs(low29 - 0x10000000) < 2048) return exp_ref_slow(x);
-    if (slow) *slow = false;
+    *slow = out_of_range | (abs(low29 - 0x10000000) < 2048);
     // float bits of y * 2^m: exponent (biased 1023 -> 127, plus m), the top
     // 23 of the 52 significand bits, plus one when the dropped bits exceed half
     const unsigned bits = ((((hi >> 20) - 896u) + static_cast<unsigned>(m)) << 23) |
                           ((hi & 0xFFFFFu) << 3) | (lo >> 29);
     return __uint_as_float(bits + (low29 > 0x10000000 ? 1u : 0u));
+}
+
+// Returns (float)exp((double)x); `tab` is the shared table. `slow`, when
+// given, is set when the call took the exp(double) path.
+__device__ __forceinline__ float exp_ref(float x, const double* tab, bool* slow = nullptr) {
+    bool s;
+    const float f = exp_ref_fast(x, tab, &s);
+    if (slow) *slow = s;
+    return s ? exp_ref_slow(x) : f;
 }
 
 }  // namespace b2

@@ -6,17 +6,19 @@
 // standalone softmax kernel (softmax_last_dim, include/tensor.h:152, is
 // declared but never defined).
 //
-// One CTA per query row (grid-stride over heads * T rows). The row's
-// in-window chunk of scores is read with 128-bit loads straight into
-// registers -- chunks wholly outside [i + 1 - window, i] are never read --
-// scaled, reduced to the max, exponentiated as the reference does --
-// (float)exp((double)d), bit for bit, through the table-driven exp_ref of
-// fastexp.cuh -- summed, divided, and the full row (zeros outside
-// the window) written with 128-bit stores. Default: tree-order denominator.
-// B2_FLAG_EXACT_ORDER: the exponentials are staged in shared memory and one
-// thread sums them in ascending key order, as the reference does, making the
-// output bit-identical.
-// HBM bound: 4 * (window cells) read + 4 * T written per row.
+// One CTA (or, for rows of <= 256 keys, one warp) per query row, grid-stride
+// over heads * T rows. The row's in-window chunk of scores is read with
+// 128-bit loads straight into registers -- chunks wholly outside
+// [i + 1 - window, i] are never read -- scaled, reduced to the max,
+// exponentiated as the reference does ((float)exp((double)d), bit for bit,
+// through the table-driven exp_ref of fastexp.cuh), summed, divided
+// (Markstein: one correctly rounded reciprocal per row), and the full row
+// (zeros outside the window) written with 128-bit stores. Default:
+// tree-order denominator. B2_FLAG_EXACT_ORDER: the exponentials are staged
+// in shared memory and one thread sums them in ascending key order, as the
+// reference does, making the output bit-identical.
+// Algorithmic bytes: 4 * (window cells) read + 4 * T written per row. At
+// T = 2048 the exponential and division work, not HBM, sets the pace.
 #include "common.cuh"
 #include "fastexp.cuh"
 
@@ -34,10 +36,27 @@ struct SoftmaxArgs {
     float scale;
 };
 
-template <int V, bool EXACT>
-__global__ void __launch_bounds__(kSmThreads)
-causal_softmax_reg(SoftmaxArgs a) {
-    __shared__ float red[2][kSmWarps];
+// e / d rounded to nearest, for 0 <= e <= 1 and a row denominator d >= 1,
+// given y = RN(1/d) (one correctly rounded reciprocal per row): with
+// q = RN(e * y) within one ulp of e / d and the residual r = e - d q exact
+// (a fused multiply-add), RN(q + r y) is the correctly rounded quotient
+// (Markstein's theorem, P. Markstein, IBM J. Res. Dev. 34(1), 1990). Three
+// FMA-pipe operations instead of a full division per element; arguments
+// below 2^-96, whose residual could leave the normal range, divide directly.
+__device__ __forceinline__ float div_by_row(float e, float d, float y) {
+    if (e < 0x1p-96f) return __fdiv_rn(e, d);
+    const float q = __fmul_rn(e, y);
+    const float r = __fmaf_rn(-d, q, e);
+    return __fmaf_rn(r, y, q);
+}
+
+// One CTA of THREADS threads per query row, V float4 per thread; block
+// reductions through shared memory.
+template <int THREADS, int V, bool EXACT>
+__global__ void __launch_bounds__(THREADS)
+causal_softmax_block(SoftmaxArgs a) {
+    constexpr int WARPS = THREADS / 32;
+    __shared__ float red[2][WARPS];
     __shared__ float denom_s;
     __shared__ double tab[64];
     extern __shared__ __align__(16) float staged[];  // EXACT: T floats
@@ -54,7 +73,7 @@ causal_softmax_reg(SoftmaxArgs a) {
         float local_max = -3.402823466e+38F;
 #pragma unroll
         for (int k = 0; k < V; ++k) {
-            const std::size_t c = threadIdx.x + static_cast<std::size_t>(k) * kSmThreads;
+            const std::size_t c = threadIdx.x + static_cast<std::size_t>(k) * THREADS;
             const std::size_t j0 = 4 * c;
             const bool any = c < T4 && j0 <= i && j0 + 3 >= begin;
             float4 s = any ? ld_stream(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -69,7 +88,7 @@ causal_softmax_reg(SoftmaxArgs a) {
                 }
             }
         }
-        const float m = block_max<kSmWarps>(local_max, red[0]);
+        const float m = block_max<WARPS>(local_max, red[0]);
         float local_sum = 0.0f;
 #pragma unroll
         for (int k = 0; k < V; ++k)
@@ -83,7 +102,7 @@ causal_softmax_reg(SoftmaxArgs a) {
         if (EXACT) {
 #pragma unroll
             for (int k = 0; k < V; ++k) {
-                const std::size_t c = threadIdx.x + static_cast<std::size_t>(k) * kSmThreads;
+                const std::size_t c = threadIdx.x + static_cast<std::size_t>(k) * THREADS;
                 if (c < T4)
                     reinterpret_cast<float4*>(staged)[c] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
             }
@@ -96,20 +115,107 @@ causal_softmax_reg(SoftmaxArgs a) {
             __syncthreads();
             denom = denom_s;
         } else {
-            denom = block_sum<kSmWarps>(local_sum, red[1]);
+            denom = block_sum<WARPS>(local_sum, red[1]);
         }
+        const float rden = __frcp_rn(denom);
 #pragma unroll
         for (int k = 0; k < V; ++k) {
-            const std::size_t c = threadIdx.x + static_cast<std::size_t>(k) * kSmThreads;
+            const std::size_t c = threadIdx.x + static_cast<std::size_t>(k) * THREADS;
             if (c < T4) {
                 float pv[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
-                    pv[e] = (valid >> (4 * k + e)) & 1u ? __fdiv_rn(v[k][e], denom) : 0.0f;
+                    pv[e] = (valid >> (4 * k + e)) & 1u ? div_by_row(v[k][e], denom, rden) : 0.0f;
                 st_plain(dst + c, make_float4(pv[0], pv[1], pv[2], pv[3]));
             }
         }
         if (EXACT) __syncthreads();  // staged[] / denom_s reused by the next row
+    }
+}
+
+
+// One warp per query row: the row's in-window 128-bit chunks go straight to
+// registers (lane l holds chunks l, l+32, ..., V per lane), max and sum are
+// warp shuffles -- no block barrier per row -- and 4 warps per CTA keep ~20
+// rows in flight per SM. EXACT stages the exponentials in the warp's slice of
+// shared memory and lane 0 sums them in ascending key order.
+constexpr int kWarpRowThreads = 128;
+constexpr int kWarpRowWarps = kWarpRowThreads / 32;
+
+template <int V, bool EXACT>
+__global__ void __launch_bounds__(kWarpRowThreads)
+causal_softmax_warp(SoftmaxArgs a) {
+    __shared__ double tab[64];
+    extern __shared__ __align__(16) float staged[];  // EXACT: kWarpRowWarps x T floats
+    load_exp2_table(tab);
+    __syncthreads();
+    const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float* mine = staged + static_cast<std::size_t>(warp) * a.T;
+    const std::size_t T4 = a.T / 4;
+    for (std::size_t row = static_cast<std::size_t>(blockIdx.x) * kWarpRowWarps + warp; row < a.rows;
+         row += static_cast<std::size_t>(gridDim.x) * kWarpRowWarps) {
+        const std::size_t i = row % a.T;
+        const std::size_t begin = i + 1 > a.window ? i + 1 - a.window : 0;
+        const float4* src = reinterpret_cast<const float4*>(a.scores + row * a.ld);
+        float4* dst = reinterpret_cast<float4*>(a.probs + row * a.ld);
+        float v[V][4];
+        unsigned long long valid = 0;  // bit 4k+e: element e of chunk k is inside the window
+        float local_max = -3.402823466e+38F;
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+            const std::size_t c = lane + 32 * static_cast<std::size_t>(k);
+            const std::size_t j0 = 4 * c;
+            const bool any = c < T4 && j0 <= i && j0 + 3 >= begin;
+            const float4 sv = any ? ld_stream(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const std::size_t j = j0 + e;
+                v[k][e] = __fmul_rn(s4[e], a.scale);
+                if (any && j >= begin && j <= i) {
+                    valid |= 1ull << (4 * k + e);
+                    local_max = fmaxf(local_max, v[k][e]);
+                }
+            }
+        }
+        const float m = warp_max(local_max);
+        float local_sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < V; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float ex = (valid >> (4 * k + e)) & 1ull ? exp_ref(__fsub_rn(v[k][e], m), tab) : 0.0f;
+                v[k][e] = ex;
+                local_sum = __fadd_rn(local_sum, ex);
+            }
+        float denom;
+        if (EXACT) {
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                const std::size_t c = lane + 32 * static_cast<std::size_t>(k);
+                if (c < T4) reinterpret_cast<float4*>(mine)[c] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
+            }
+            __syncwarp();
+            float d = 0.0f;
+            if (lane == 0)
+                for (std::size_t j = begin; j <= i; ++j) d = __fadd_rn(d, mine[j]);
+            denom = __shfl_sync(0xffffffffu, d, 0);
+        } else {
+            denom = warp_sum(local_sum);
+        }
+        const float rden = __frcp_rn(denom);
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+            const std::size_t c = lane + 32 * static_cast<std::size_t>(k);
+            if (c < T4) {
+                float pv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    pv[e] = (valid >> (4 * k + e)) & 1ull ? div_by_row(v[k][e], denom, rden) : 0.0f;
+                st_plain(dst + c, make_float4(pv[0], pv[1], pv[2], pv[3]));
+            }
+        }
+        if (EXACT) __syncwarp();  // the warp's staging slice is reused by its next row
     }
 }
 
@@ -154,20 +260,33 @@ causal_softmax_smem(SoftmaxArgs a) {
         } else {
             denom = block_sum<kSmWarps>(local_sum, red[1]);
         }
+        const float rden = __frcp_rn(denom);
         for (std::size_t j = threadIdx.x; j < a.T; j += kSmThreads)
-            dst[j] = (j >= begin && j <= i) ? __fdiv_rn(staged[j], denom) : 0.0f;
+            dst[j] = (j >= begin && j <= i) ? div_by_row(staged[j], denom, rden) : 0.0f;
         __syncthreads();
     }
 }
 
-template <int V, bool EXACT>
-int launch_reg(const SoftmaxArgs& a, cudaStream_t s) {
+template <int THREADS, int V, bool EXACT>
+int launch_block(const SoftmaxArgs& a, cudaStream_t s) {
     const std::size_t smem = EXACT ? a.T * sizeof(float) : 0;
-    auto kernel = causal_softmax_reg<V, EXACT>;
+    auto kernel = causal_softmax_block<THREADS, V, EXACT>;
     if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("causal softmax: shared memory attribute");
-    const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), kSmThreads, smem, a.rows);
-    kernel<<<grid, kSmThreads, smem, s>>>(a);
+    const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), THREADS, smem, a.rows);
+    kernel<<<grid, THREADS, smem, s>>>(a);
+    return B2_OK;
+}
+
+template <int V, bool EXACT>
+int launch_warp(const SoftmaxArgs& a, cudaStream_t s) {
+    const std::size_t smem = EXACT ? kWarpRowWarps * a.T * sizeof(float) : 0;
+    auto kernel = causal_softmax_warp<V, EXACT>;
+    if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
+        return launch_result("causal softmax: shared memory attribute");
+    const std::size_t blocks = (a.rows + kWarpRowWarps - 1) / kWarpRowWarps;
+    const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), kWarpRowThreads, smem, blocks);
+    kernel<<<grid, kWarpRowThreads, smem, s>>>(a);
     return B2_OK;
 }
 
@@ -182,14 +301,18 @@ int launch_smem(const SoftmaxArgs& a, cudaStream_t s) {
     return B2_OK;
 }
 
+// Short rows (T <= 256) take a warp each; longer rows a CTA each. Measured
+// at T = 2048 on B200: 128 threads x 4 float4 per thread beats 256 x 2,
+// 512 x 1 and a warp per row (16 float4 per lane: too many registers).
 template <bool EXACT>
 int dispatch(const SoftmaxArgs& a, bool vec, cudaStream_t s) {
     const std::size_t T4 = a.T / 4;
-    if (vec && T4 <= 8 * kSmThreads) {
-        if (T4 <= kSmThreads) return launch_reg<1, EXACT>(a, s);
-        if (T4 <= 2 * kSmThreads) return launch_reg<2, EXACT>(a, s);
-        if (T4 <= 4 * kSmThreads) return launch_reg<4, EXACT>(a, s);
-        return launch_reg<8, EXACT>(a, s);
+    if (vec) {
+        if (T4 <= 32) return launch_warp<1, EXACT>(a, s);
+        if (T4 <= 64) return launch_warp<2, EXACT>(a, s);
+        if (T4 <= 512) return launch_block<128, 4, EXACT>(a, s);
+        if (T4 <= 1024) return launch_block<256, 4, EXACT>(a, s);
+        if (T4 <= 2048) return launch_block<256, 8, EXACT>(a, s);
     }
     return launch_smem<EXACT>(a, s);
 }

@@ -211,18 +211,23 @@ class Pipeline:
         self._layers = arr
         self._standins = list(standins)
 
-    def run(self, stream=None, timer: "StageTimer | None" = None) -> None:
+    def run(self, stream=None, timer: "StageTimer | None" = None, final_out: torch.Tensor | None = None) -> None:
         """Enqueues all layers + the final LayerNorm on `stream` (default:
-        the current torch stream); `timer` records per-launch events."""
+        the current torch stream); `timer` records per-launch events;
+        `final_out` redirects the final LayerNorm output (e.g. straight into
+        a send buffer when node rows are token rows)."""
         if self._layers is None:
             raise RuntimeError("bind_layers() first")
         st = stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream
         w = self.weights
         ev = timer.handles() if timer is not None else None
+        out = self.final_out if final_out is None else final_out
+        if out.numel() != self.final_out.numel() or out.dtype != torch.float32 or not out.is_contiguous():
+            raise ops.InvalidArgument("final_out shape")
         rc = self._fn(C.addressof(self.shape), w.emb.data_ptr(), w.emb.shape[0], self.batch.node_token.data_ptr(),
                       self.batch.node_depth.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(), self.cos.shape[0],
                       C.addressof(self._layers), len(self._layers), w.final[0].data_ptr(), w.final[1].data_ptr(),
-                      C.addressof(self.work), self.final_x.data_ptr(), self.final_out.data_ptr(),
+                      C.addressof(self.work), self.final_x.data_ptr(), out.data_ptr(),
                       C.addressof(ev) if ev is not None else None, st)
         ops._check(rc, "b2_prefill_layers")
 
@@ -233,6 +238,105 @@ class Pipeline:
     def last_token_rows(self, out: torch.Tensor) -> None:
         """Final hidden state of each prompt's last token (the lm_head input)."""
         ops.gather_rows_gpu(self.final_out, self.batch.last_rows, out)
+
+
+def identity_rows(batch: Batch) -> bool:
+    """True when every token row is its own trie node in order (no shared
+    prefixes): the final node rows are then already the token rows."""
+    tn = batch.trie.token_node
+    return batch.rows == tn.size and bool((tn == np.arange(tn.size, dtype=tn.dtype)).all())
+
+
+def slice_standins(s: StandIns, r0: int, rows: int) -> StandIns:
+    """Row range [r0, r0 + rows) of a stand-in set (assignment-ordered
+    tensors use rows [2 r0, 2 (r0 + rows)))."""
+    return StandIns(s.q[r0:r0 + rows], s.k[r0:r0 + rows], s.attn[r0:r0 + rows], s.logits[r0:r0 + rows],
+                    s.gate_up[2 * r0:2 * (r0 + rows)], s.expert_out[2 * r0:2 * (r0 + rows)])
+
+
+class ShardedPrefill:
+    """One rank's share of a prompt batch on one GPU, split into `chunks`
+    sub-batches. Each chunk runs all layers (b2_prefill_layers), writes its
+    final hidden states as token rows, and -- with world > 1 -- is gathered
+    to rank 0 by NCCL on the collective's own stream while the next chunk
+    computes, so only the last chunk's gather is exposed."""
+
+    def __init__(self, prompts: Sequence[np.ndarray], plan: list, weights: Weights, device,
+                 standins: Sequence[StandIns], layers: int, rank: int = 0, exact: bool = False, group=None):
+        """`plan` is shard.chunk_plan(prompts, world, chunks): this rank runs
+        plan[rank]; every rank's chunk c must have the same token count (the
+        per-chunk gather moves equal-sized buffers)."""
+        self.device, self.world, self.rank, self.group = device, len(plan), rank, group
+        world = self.world
+        self.layers = layers
+        self.plan = plan
+        self.parts = plan[rank]
+        self.prompts = [[prompts[i] for i in part] for part in self.parts]
+        self.all_prompts = prompts
+        self.batches = [Batch.build(ps, device) for ps in self.prompts]
+        self.pipes, self.send, self.direct = [], [], []
+        r0 = 0
+        for b in self.batches:
+            pipe = Pipeline(b, weights, device, exact=exact)
+            pipe.bind_layers([slice_standins(s, r0, b.rows) for s in standins], layers)
+            self.pipes.append(pipe)
+            self.send.append(torch.empty((b.tokens, HIDDEN), device=device))
+            self.direct.append(identity_rows(b))
+            r0 += b.rows
+        self.rows = r0
+        self.tokens = sum(b.tokens for b in self.batches)
+        self.recv = None
+        if world > 1 and rank == 0:
+            self.recv = [[torch.empty_like(t) for _ in range(world)] for t in self.send]
+
+    @staticmethod
+    def rows_needed(prompts: Sequence[np.ndarray], parts: list) -> int:
+        return sum(ops.prefix_trie([prompts[i] for i in part]).nodes for part in parts)
+
+    def launches_per_step(self) -> int:
+        return sum(launches_per_run(self.layers) + (0 if d else 1) for d in self.direct)
+
+    def step(self, timers=None) -> None:
+        """Enqueues the whole share on the current stream (+ the gathers);
+        on return the current stream is ordered after every gather."""
+        import torch.distributed as dist
+
+        works = []
+        for c, pipe in enumerate(self.pipes):
+            if self.direct[c]:
+                pipe.run(timer=timers[c] if timers else None, final_out=self.send[c])
+            else:
+                pipe.run(timer=timers[c] if timers else None)
+                pipe.expand_to_tokens(self.send[c])
+            if self.world > 1:
+                works.append(dist.gather(self.send[c], self.recv[c] if self.rank == 0 else None, dst=0,
+                                         group=self.group, async_op=True))
+        for w in works:
+            w.wait()
+
+    def rebuild(self, pinned: bool = True) -> int:
+        """The host part of an end-to-end step: rebuilds every chunk's trie
+        from host token ids and uploads its index arrays; returns the H2D
+        bytes."""
+        nbytes = 0
+        for c, ps in enumerate(self.prompts):
+            b = Batch.build(ps, self.device, pinned=pinned)
+            self.pipes[c].batch = b
+            self.batches[c] = b
+            nbytes += sum(int(t.numel()) * 4 for t in (b.node_token, b.node_depth, b.token_node, b.last_rows))
+        return nbytes
+
+    def last_token_rows(self, out: torch.Tensor) -> None:
+        """Rank 0, after step(): the final hidden state of every prompt's last
+        token, for all ranks' prompts, in shard.gather_order(plan) order."""
+        k = 0
+        for c in range(len(self.batches)):
+            for r in range(self.world):
+                ends = np.cumsum([len(self.all_prompts[i]) for i in self.plan[r][c]]) - 1
+                idx = torch.from_numpy(ends.astype(np.int32)).to(self.device)
+                src = self.recv[c][r] if self.recv is not None else self.send[c]
+                ops.gather_rows_gpu(src, idx, out[k:k + ends.size])
+                k += ends.size
 
 
 class StageTimer:

@@ -29,3 +29,25 @@ def shard_prompts(prompts: Sequence[Sequence[int]], world: int) -> list[list[int
         out[r].extend(g)
         load[r] += sum(len(prompts[i]) for i in g)
     return [sorted(x) for x in out]
+
+
+def chunk_plan(prompts: Sequence[Sequence[int]], world: int, chunks: int) -> list[list[list[int]]]:
+    """plan[rank][chunk] = global prompt indices: the rank shards of
+    shard_prompts, each split again into `chunks` sub-batches the same way
+    (empty sub-batches dropped)."""
+    plan = []
+    for mine in shard_prompts(prompts, world):
+        sub = shard_prompts([prompts[i] for i in mine], chunks) if mine else []
+        plan.append([[mine[j] for j in part] for part in sub if part])
+    return plan
+
+
+def gather_order(plan: list[list[list[int]]]) -> list[int]:
+    """Global prompt indices in the order rank 0 holds them after the
+    per-chunk gathers: chunk-major, then rank, then prompt."""
+    order: list[int] = []
+    for c in range(max((len(p) for p in plan), default=0)):
+        for r in range(len(plan)):
+            if c < len(plan[r]):
+                order.extend(plan[r][c])
+    return order

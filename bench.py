@@ -36,9 +36,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "non-GEMM prefill tokens/s (64x2048 prompts, 32 layers; layer-op HBM GB/s in roofline)"
-# DRAM bytes per launch of the dominant kernel, from the ncu capture in
-# profiles/fused_combine_add_ln.md (per node row; scaled by rows).
-TRAFFIC_BYTES_PER_ROW = None
+# DRAM bytes (read + write) per node row of a kernel launch, from one ncu
+# capture of that kernel on a smaller case of the same workload (8192 rows;
+# profiles/fused_combine_add_ln_config5.md), scaled to a launch by rows.
+TRAFFIC_BYTES_PER_ROW = {"fused": (402.787072e6 + 212.106752e6) / 8192}
 
 
 def parse():
@@ -52,6 +53,7 @@ def parse():
     p.add_argument("--length", type=int, default=2048)
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--pool", type=int, default=0, help="stand-in sets (0 = fit to memory)")
+    p.add_argument("--chunks", type=int, default=0, help="sub-batches per rank (0 = 1 on one GPU, 2 otherwise)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -148,20 +150,14 @@ def dist_setup(n_gpus: int):
     return rank, world, local
 
 
-def shard(prompts, rank: int, world: int) -> list[int]:
-    from aps2026_b200.shard import shard_prompts
-
-    return shard_prompts(prompts, world)[rank]
-
-
 # ---- our arm --------------------------------------------------------------------------------
 
 
 def run_ours(args):
     import torch
 
-    from aps2026_b200 import ops, prefill
-    from aps2026_b200.prefill import Batch, Pipeline, StageTimer, StandIns, Weights
+    from aps2026_b200 import prefill
+    from aps2026_b200.prefill import ShardedPrefill, StageTimer, StandIns, Weights
 
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
@@ -169,50 +165,36 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
 
+    from aps2026_b200.shard import chunk_plan
+
     prompts = prefill.prompts_config5(batch=args.prompts, length=args.length)
-    mine = shard(prompts, rank, world)
-    my_prompts = [prompts[i] for i in mine]
     tokens_total = sum(len(p) for p in prompts)
+    chunks = args.chunks or (1 if world == 1 else 2)
+    plan = chunk_plan(prompts, world, chunks)
+    sizes = {tuple(sum(len(prompts[i]) for i in part) for part in parts) for parts in plan}
+    if len(sizes) != 1:
+        raise SystemExit("unequal shards: the per-chunk gather expects equal token counts on every rank")
 
     weights = Weights.make(dev, seed=4, layers=args.layers)
-    batch = Batch.build(my_prompts, dev)
-    R = batch.rows
-    pipe = Pipeline(batch, weights, dev, exact=args.exact)
+    rows = ShardedPrefill.rows_needed(prompts, plan[rank])
     free, _ = torch.cuda.mem_get_info(dev)
-    set_bytes = prefill.standin_bytes(R)
-    gather_bytes = (tokens_total if rank == 0 else 0) * prefill.HIDDEN * 4 + batch.tokens * prefill.HIDDEN * 4
-    pool = args.pool or int(max(1, min(args.layers, 8 if world == 1 else 32,
-                                       (free * 0.75 - gather_bytes) // set_bytes)))
+    set_bytes = prefill.standin_bytes(rows)
+    own = rows * prefill.HIDDEN * 4 * 7 + (tokens_total * prefill.HIDDEN * 4 if rank == 0 else 0)
+    pool = args.pool or int(max(1, min(args.layers, 8 if world == 1 else 32, (free * 0.8 - own) // set_bytes)))
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     t_gen = time.perf_counter()
-    standins = [StandIns.make(R, dev, gen) for _ in range(pool)]
+    standins = [StandIns.make(rows, dev, gen) for _ in range(pool)]
     torch.cuda.synchronize()
     t_gen = time.perf_counter() - t_gen
-    pipe.bind_layers(standins, args.layers)
-
-    # the step's collective: final hidden states of every token row to rank 0
-    send = torch.empty((batch.tokens, prefill.HIDDEN), device=dev)
-    shard_tokens = max(sum(len(prompts[i]) for i in shard(prompts, r, world)) for r in range(world))
-    if world > 1 and batch.tokens != shard_tokens:
-        raise SystemExit("unequal shards: the gather below expects equal token counts per rank")
-    recv = [torch.empty_like(send) for _ in range(world)] if (world > 1 and rank == 0) else None
-    last = torch.empty((len(my_prompts), prefill.HIDDEN), device=dev)
+    runner = ShardedPrefill(prompts, plan, weights, dev, standins, args.layers, rank=rank, exact=args.exact)
     stream = torch.cuda.current_stream(dev)
 
-    def step(timer=None):
-        pipe.run(timer=timer)
-        pipe.expand_to_tokens(send)
-        if world > 1:
-            dist.gather(send, recv, dst=0)
-
-    launches_per_step = prefill.launches_per_run(args.layers) + 1
-
     for _ in range(args.warmup):
-        step()
+        runner.step()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    timers = [StageTimer(args.layers) for _ in range(args.steps)]
+    timers = [[StageTimer(args.layers) for _ in runner.pipes] for _ in range(args.steps)]
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
@@ -220,7 +202,7 @@ def run_ours(args):
             dist.barrier()
         ev[0].record(stream)
         for k in range(args.steps):
-            step(timers[k])
+            runner.step(timers[k])
             ev[k + 1].record(stream)
         torch.cuda.synchronize()
         if dist:
@@ -233,70 +215,66 @@ def run_ours(args):
     ms_per_step = ms / args.steps
 
     # per-kernel durations inside the timed region (this rank)
-    dur = {}
-    for tm in timers:
-        for k, v in tm.durations().items():
-            dur.setdefault(k, []).extend(v)
     bpr = prefill.bytes_per_row(args.layers)
-    kern = {}
-    for k, v in dur.items():
-        per_launch_ms = statistics.mean(v)
-        total_ms = sum(v) / args.steps
-        nbytes = bpr[k if k in bpr else "ln0"] * R
-        kern[k] = dict(launches_per_step=len(v) // args.steps, ms_per_step=round(total_ms, 4),
-                       us_per_launch=round(per_launch_ms * 1e3, 2),
-                       gbs=round(nbytes / (per_launch_ms * 1e-3) / 1e9, 1))
+    acc = {}
+    for step_timers in timers:
+        for c, tm in enumerate(step_timers):
+            rows_c = runner.batches[c].rows
+            for kind, vals in tm.durations().items():
+                a = acc.setdefault(kind, [0, 0.0, 0.0])
+                a[0] += len(vals)
+                a[1] += sum(vals)
+                a[2] += bpr[kind if kind in bpr else "ln0"] * rows_c * len(vals)
+    kern = {kind: dict(launches_per_step=n // args.steps, ms_per_step=round(t / args.steps, 4),
+                       us_per_launch=round(t / n * 1e3, 2), gbs=round(b / (t * 1e-3) / 1e9, 1))
+            for kind, (n, t, b) in acc.items()}
     dominant = max(kern, key=lambda k: kern[k]["ms_per_step"])
 
-    # e2e: host ids -> trie -> H2D -> layers -> gather -> D2H of last-token rows
-    ids_pinned = [torch.from_numpy(p).pin_memory() for p in my_prompts]
-    host_last = torch.empty((len(my_prompts), prefill.HIDDEN), pin_memory=True)
+    # e2e: host ids -> tries -> H2D -> layers -> gather -> D2H of last-token rows
+    last = torch.empty((args.prompts, prefill.HIDDEN), device=dev)
+    host_last = torch.empty((args.prompts, prefill.HIDDEN), pin_memory=True)
 
     def e2e_step():
-        ids = [t.numpy() for t in ids_pinned]
-        b = Batch.build(ids, dev, pinned=True)
-        pipe.batch = b
-        step()
-        pipe.last_token_rows(last)
+        h2d = runner.rebuild(pinned=True)
+        runner.step()
         if rank == 0:
+            runner.last_token_rows(last)
             host_last.copy_(last, non_blocking=True)
-        return b
+        return h2d
 
-    e2e_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    for _ in range(1):
-        e2e_step()
+    e2e_step()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     e2e_steps = max(1, min(args.steps, 3))
+    e2e_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     e2e_ev[0].record(stream)
     for _ in range(e2e_steps):
-        b = e2e_step()
+        h2d = e2e_step()
     e2e_ev[1].record(stream)
     torch.cuda.synchronize()
     e2e_ms = e2e_ev[0].elapsed_time(e2e_ev[1]) / e2e_steps
+    h2d_all = h2d
     if dist:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    h2d = sum(int(x.numel()) * 4 for x in (b.node_token, b.node_depth, b.token_node, b.last_rows))
+        t = torch.tensor([e2e_ms, float(h2d)], device=dev, dtype=torch.float64)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        e2e_ms, h2d_all = float(mx[0].item()), int(t[1].item())
     d2h = host_last.numel() * 4 if rank == 0 else 0
 
     clk = clocks.summary()
+    allclk = [clk]
     if dist:
         allclk = [None] * world
         dist.all_gather_object(allclk, clk)
-        kern_all = [None] * world
-        dist.all_gather_object(kern_all, kern)
-    else:
-        allclk = [clk]
 
     result = None
     if rank == 0:
         peak, peak_kind = peaks()
         d = kern[dominant]
-        achieved = d["gbs"]
-        traffic = (TRAFFIC_BYTES_PER_ROW * R) if TRAFFIC_BYTES_PER_ROW else None
+        traffic = (round(TRAFFIC_BYTES_PER_ROW[dominant] * rows / len(runner.pipes))
+                   if dominant in TRAFFIC_BYTES_PER_ROW else None)
         reasons = sorted(set(r for c in allclk for r in c.get("reasons", [])))
         mhz = [c["sm_mhz"] for c in allclk if c.get("sm_mhz")]
         tok_s = tokens_total / (ms_per_step / 1e3)
@@ -316,24 +294,25 @@ def run_ours(args):
             "config": {"workload": f"config 5: {args.prompts} prompts x {args.length} tokens, {args.layers} layers, "
                                    "non-GEMM path, final hidden states gathered to rank 0",
                        "prompts": args.prompts, "tokens_per_prompt": args.length, "layers": args.layers,
-                       "node_rows_per_rank": R, "standin_pool": pool, "exact_order": args.exact,
+                       "node_rows_per_rank": rows, "chunks_per_rank": len(runner.pipes), "standin_pool": pool,
+                       "exact_order": args.exact,
                        "l2": "inputs larger than L2 (every kernel streams >= 100 MB per launch)",
-                       "parallelism": f"prompt shards x{world}" + (", NCCL gather to rank 0" if world > 1 else "")},
-            "hbm_gbs_algorithmic": round(bpr["total"] * R * world / (ms_per_step / 1e3) / 1e9, 1),
-            "roofline": {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 3), "peak_kind": peak_kind,
+                       "parallelism": f"prompt shards x{world}" + (", NCCL gather to rank 0 overlapped by chunk"
+                                                                  if world > 1 else "")},
+            "hbm_gbs_algorithmic": round(bpr["total"] * rows * world / (ms_per_step / 1e3) / 1e9, 1),
+            "roofline": {"kernel": dominant, "bound": "hbm", "achieved": d["gbs"], "peak": peak,
+                         "unit": "GB/s", "frac": round(d["gbs"] / peak, 3), "peak_kind": peak_kind,
                          "traffic": traffic},
             "kernels": kern,
             "clocks": {"sm_mhz": statistics.median(mhz) if mhz else None,
                        "sm_max_mhz": allclk[0].get("sm_max_mhz"), "reasons": reasons},
             "e2e": {"value": round(tokens_total / (e2e_ms / 1e3), 1), "unit": "tokens/s",
-                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h},
-            "gpu_launches": launches_per_step * args.steps * world,
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h},
+            "gpu_launches": runner.launches_per_step() * args.steps * world,
             "standin_gen_s": round(t_gen, 2),
         }
     if dist:
-        recv = None
+        runner.recv = None
         dist.barrier()
         dist.destroy_process_group()
     return result

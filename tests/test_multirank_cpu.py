@@ -1,0 +1,124 @@
+"""Multi-rank prefill on CPU ranks (gloo, world size 2): prompt sharding, one
+trie per chunk, per-rank layer pipelines and the gather of final hidden
+states to rank 0 reproduce the single-process result row for row.
+
+Each rank runs the CPU oracle's layer pipeline on its chunks (the GPU ranks
+run b2_prefill_layers with the same plan) and rank 0 collects the chunks with
+torch.distributed.gather in shard.gather_order; the GEMM stand-ins are a
+fixed function of (prompt, position), so sharding cannot change any row.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+HID, QH, KVH, HD, INTER, LAYERS = 32, 2, 1, 8, 16, 2
+
+
+def _prompts():
+    g = np.random.default_rng(40)
+    ps = [g.integers(0, 500, int(g.integers(8, 14))).astype(np.int32) for _ in range(8)]
+    for i in range(1, 8, 2):  # pairs of prompts of equal length keep the rank shards equal in tokens
+        ps[i] = g.integers(0, 500, len(ps[i - 1])).astype(np.int32)
+    return ps
+
+
+def _standin_rows(prompt_idx: int, length: int) -> dict:
+    """Per-token GEMM stand-ins of one prompt. expert_out holds each token's
+    two expert rows in slot order; the batch places them at the token's
+    route positions, as the grouped W2 GEMM would."""
+    g = np.random.default_rng(1000 + prompt_idx)
+    n = lambda *s: g.standard_normal(s).astype(np.float32)  # noqa: E731
+    return dict(q=n(length, QH * HD), k=n(length, KVH * HD), attn=n(length, HID), logits=n(length, 16),
+                gate_up=n(2 * length, 2 * INTER), expert_out=n(2 * length, HID))
+
+
+def _weights():
+    g = np.random.default_rng(41)
+    n = lambda *s: g.standard_normal(s).astype(np.float32)  # noqa: E731
+    emb = (0.02 * n(500, HID)).astype(np.float32)
+    ln = lambda: (1 + 0.1 * n(HID), 0.1 * n(HID))  # noqa: E731
+    return emb, [ln() for _ in range(LAYERS)], [ln() for _ in range(LAYERS)], ln()
+
+
+def _run_chunk(prompts, idx):
+    """Final hidden states (token rows) of the prompts `idx`, by the oracle."""
+    import oracle
+
+    sub = [prompts[i] for i in idx]
+    trie = oracle.prefix_trie(sub, vocab=500)
+    assert trie["nodes"] == sum(len(p) for p in sub)  # no shared prefixes: node rows are token rows
+    rows = {k: [] for k in ("q", "k", "attn", "logits", "gate_up", "expert_out")}
+    for i in idx:
+        s = _standin_rows(i, len(prompts[i]))
+        for k in rows:
+            rows[k].append(s[k])
+    standin = {k: np.ascontiguousarray(np.concatenate(v)) for k, v in rows.items()}
+    # token t's slot-s expert row goes to its route position in this batch
+    rp = oracle.moe_route(standin["logits"])["route_positions"]
+    placed = np.empty_like(standin["expert_out"])
+    placed[rp] = standin["expert_out"]
+    standin["expert_out"] = placed
+    emb, ln1, ln2, fin = _weights()
+    _, y = oracle.prefill_layers(emb, trie["node_token"], trie["node_depth"], [standin], ln1, ln2, fin, LAYERS,
+                                 q_heads=QH, kv_heads=KVH, head_dim=HD, inter=INTER)
+    return y[trie["token_node"]]
+
+
+def _rank_main(rank, world, port, out_path):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from aps2026_b200.shard import chunk_plan
+
+        prompts = _prompts()
+        plan = chunk_plan(prompts, world, 2)
+        for c, idx in enumerate(plan[rank]):
+            send = torch.from_numpy(_run_chunk(prompts, idx))
+            recv = [torch.empty_like(send) for _ in range(world)] if rank == 0 else None
+            dist.gather(send, recv, dst=0)
+            if rank == 0:
+                np.save(f"{out_path}.{c}.npy", torch.cat(recv).numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_chunk_plan_covers_every_prompt_once():
+    from aps2026_b200.shard import chunk_plan, gather_order, shard_prompts
+
+    prompts = _prompts()
+    for world in (1, 2, 3, 8):
+        plan = chunk_plan(prompts, world, 2)
+        flat = sorted(i for parts in plan for part in parts for i in part)
+        assert flat == list(range(len(prompts)))
+        assert sorted(gather_order(plan)) == flat
+    # shared first tokens stay on one rank
+    same = [np.array([7, 1, 2]), np.array([7, 1, 3]), np.array([9, 9]), np.array([5])]
+    shards = shard_prompts(same, 2)
+    assert any({0, 1} <= set(s) for s in shards)
+
+
+def test_two_cpu_ranks_gather_matches_single_process(tmp_path):
+    from aps2026_b200.shard import chunk_plan, gather_order
+
+    world = 2
+    out = str(tmp_path / "gathered")
+    mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
+    prompts = _prompts()
+    plan = chunk_plan(prompts, world, 2)
+    got = np.concatenate([np.load(f"{out}.{c}.npy") for c in range(len(plan[0]))])
+    order = gather_order(plan)
+    want = np.concatenate([_run_chunk(prompts, [i]) for i in order])
+    np.testing.assert_array_equal(got, want)
