@@ -63,6 +63,37 @@ inline cudaError_t allow_dynamic_smem(const void* kernel, std::size_t bytes) {
                                 static_cast<int>(bytes));
 }
 
+// ---- programmatic dependent launch ---------------------------------------------
+//
+// Every kernel is launched with programmatic stream serialization: its CTAs
+// may be scheduled while the previous kernel on the stream drains, which
+// hides the launch gap and the previous grid's tail. pdl_begin() is the
+// first statement of every kernel: it waits until the previous grid has
+// completed and its writes are visible (griddepcontrol.wait -- a hardware
+// dependency, not a spin), then lets the next kernel start its own launch.
+// When the previous kernel was not launched this way (or there is none),
+// the wait returns at once.
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, std::size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---- in-kernel bounds checks -------------------------------------------------
 //
 // Every kernel that dereferences a caller-provided index checks it, skips

@@ -19,6 +19,7 @@ __global__ void __launch_bounds__(kGatherThreads)
 gather_rows_vec(const float4* __restrict__ x, std::size_t x_rows, std::size_t h4,
                 const std::uint32_t* __restrict__ rows, std::size_t count,
                 float4* __restrict__ out) {
+    pdl_begin();
     for (std::size_t i = blockIdx.x; i < count; i += gridDim.x) {
         const std::uint32_t src = __ldg(rows + i);
         float4* dst = out + i * h4;
@@ -50,6 +51,7 @@ __global__ void __launch_bounds__(kGatherThreads)
 gather_rows_scalar(const float* __restrict__ x, std::size_t x_rows, std::size_t h,
                    const std::uint32_t* __restrict__ rows, std::size_t count,
                    float* __restrict__ out) {
+    pdl_begin();
     for (std::size_t i = blockIdx.x; i < count; i += gridDim.x) {
         const std::uint32_t src = __ldg(rows + i);
         float* dst = out + i * h;
@@ -79,13 +81,13 @@ extern "C" int b2_gather_rows(const float* x, size_t x_rows, size_t h,
     if ((h & 3u) == 0 && aligned16(x) && aligned16(out)) {
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(gather_rows_vec),
                                         kGatherThreads, 0, count);
-        gather_rows_vec<<<grid, kGatherThreads, 0, s>>>(
+        launch_pdl(gather_rows_vec, grid, kGatherThreads, 0, s, 
             reinterpret_cast<const float4*>(x), x_rows, h / 4, rows, count,
             reinterpret_cast<float4*>(out));
     } else {
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(gather_rows_scalar),
                                         kGatherThreads, 0, count);
-        gather_rows_scalar<<<grid, kGatherThreads, 0, s>>>(x, x_rows, h, rows, count, out);
+        launch_pdl(gather_rows_scalar, grid, kGatherThreads, 0, s, x, x_rows, h, rows, count, out);
     }
     return launch_result("b2_gather_rows");
 }

@@ -136,6 +136,7 @@ __device__ __forceinline__ float4 load_chunk(const LnArgs& a, std::size_t r, std
 template <int MODE, int THREADS, int V, bool EXACT>
 __global__ void __launch_bounds__(THREADS)
 ln_rows_reg(LnArgs a) {
+    pdl_begin();
     constexpr int WARPS = THREADS / 32;
     __shared__ float red[2][WARPS];
     __shared__ float stats[2];
@@ -201,6 +202,7 @@ ln_rows_reg(LnArgs a) {
 template <int MODE, bool EXACT>
 __global__ void __launch_bounds__(256)
 ln_rows_smem(LnArgs a) {
+    pdl_begin();
     constexpr int THREADS = 256, WARPS = 8;
     __shared__ float red[2][WARPS];
     __shared__ float stats[2];
@@ -258,7 +260,7 @@ int launch_reg(const LnArgs& a, cudaStream_t s) {
     if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("layer norm: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), THREADS, smem, a.rows);
-    kernel<<<grid, THREADS, smem, s>>>(a);
+    launch_pdl(kernel, grid, THREADS, smem, s, a);
     return B2_OK;
 }
 
@@ -269,7 +271,7 @@ int launch_smem(const LnArgs& a, cudaStream_t s) {
     if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("layer norm: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), 256, smem, a.rows);
-    kernel<<<grid, 256, smem, s>>>(a);
+    launch_pdl(kernel, grid, 256, smem, s, a);
     return B2_OK;
 }
 

@@ -68,6 +68,7 @@ __device__ __forceinline__ float quantize(float s, float quantum) {
 
 __global__ void __launch_bounds__(kTile)
 route_select(RouteArgs a) {
+    pdl_begin();
     __shared__ unsigned int hist[kMaxExperts];
     const unsigned E = static_cast<unsigned>(a.E);
     if (threadIdx.x < kMaxExperts) hist[threadIdx.x] = 0;
@@ -133,6 +134,7 @@ __device__ __forceinline__ uint4 shfl_xor_u4(const uint4& v, int o) {
 
 __global__ void __launch_bounds__(kTile)
 route_scatter(RouteArgs a) {
+    pdl_begin();
     constexpr int WARPS = kTile / 32;
     __shared__ uint4 red_all[WARPS][kMaxExperts / 4], red_before[WARPS][kMaxExperts / 4];
     __shared__ unsigned int base_s[kMaxExperts], offs_s[kMaxExperts + 1];
@@ -301,6 +303,7 @@ __global__ void __launch_bounds__(kSiluThreads, 4)
 silu_mul_vec(const float* __restrict__ gate, std::size_t ldg, const float* __restrict__ up,
              std::size_t ldu, float* __restrict__ out, std::size_t ldo, std::size_t rows,
              std::size_t c4) {
+    pdl_begin();
     __shared__ double tab[64];
     load_exp2_table(tab);
     __syncthreads();
@@ -328,6 +331,7 @@ __global__ void __launch_bounds__(kSiluThreads)
 silu_mul_scalar(const float* __restrict__ gate, std::size_t ldg, const float* __restrict__ up,
                 std::size_t ldu, float* __restrict__ out, std::size_t ldo, std::size_t rows,
                 std::size_t cols) {
+    pdl_begin();
     __shared__ double tab[64];
     load_exp2_table(tab);
     __syncthreads();
@@ -349,6 +353,7 @@ moe_combine_rows(const float* __restrict__ expert_out, std::size_t expert_rows,
                  const std::uint8_t* __restrict__ routes,
                  const std::uint32_t* __restrict__ route_positions, float* __restrict__ out,
                  std::size_t T, std::size_t h) {
+    pdl_begin();
     for (std::size_t t = blockIdx.x; t < T; t += gridDim.x) {
         const CombineRows cr = combine_rows(routes, route_positions, t, expert_rows);
         if (VEC) {
@@ -385,6 +390,7 @@ moe_combine_rows(const float* __restrict__ expert_out, std::size_t expert_rows,
 
 __global__ void __launch_bounds__(256)
 add_vec(float4* __restrict__ a, const float4* __restrict__ b, std::size_t n4) {
+    pdl_begin();
     const std::size_t stride = static_cast<std::size_t>(gridDim.x) * 256;
     for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * 256 + threadIdx.x; i < n4; i += stride * 2) {
         const std::size_t i2 = i + stride;
@@ -401,6 +407,7 @@ add_vec(float4* __restrict__ a, const float4* __restrict__ b, std::size_t n4) {
 
 __global__ void __launch_bounds__(256)
 add_scalar(float* __restrict__ a, const float* __restrict__ b, std::size_t n) {
+    pdl_begin();
     const std::size_t stride = static_cast<std::size_t>(gridDim.x) * 256;
     for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * 256 + threadIdx.x; i < n; i += stride)
         a[i] = __fadd_rn(a[i], b[i]);
@@ -449,8 +456,8 @@ int b2_moe_route(const float* logits, size_t T, size_t E, float quantum, float t
     a.tiles = route_tiles(T);
     if (a.tiles > 0x7FFFFFFFu) return invalid("b2_moe_route: too many tiles");
     cudaStream_t s = as_stream(stream);
-    route_select<<<static_cast<unsigned>(a.tiles), kTile, 0, s>>>(a);
-    route_scatter<<<static_cast<unsigned>(a.tiles), kTile, 0, s>>>(a);
+    launch_pdl(route_select, static_cast<unsigned>(a.tiles), kTile, 0, s, a);
+    launch_pdl(route_scatter, static_cast<unsigned>(a.tiles), kTile, 0, s, a);
     return launch_result("b2_moe_route");
 }
 
@@ -468,10 +475,10 @@ int b2_silu_mul(const float* gate, size_t ld_gate, const float* up, size_t ld_up
         const std::size_t chunks = rows * (cols / 4);
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(silu_mul_vec), kSiluThreads, 0,
                                         (chunks + kSiluThreads - 1) / kSiluThreads);
-        silu_mul_vec<<<grid, kSiluThreads, 0, s>>>(gate, ld_gate, up, ld_up, out, ld_out, rows, cols / 4);
+        launch_pdl(silu_mul_vec, grid, kSiluThreads, 0, s, gate, ld_gate, up, ld_up, out, ld_out, rows, cols / 4);
     } else {
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(silu_mul_scalar), kSiluThreads, 0, blocks_needed);
-        silu_mul_scalar<<<grid, kSiluThreads, 0, s>>>(gate, ld_gate, up, ld_up, out, ld_out, rows, cols);
+        launch_pdl(silu_mul_scalar, grid, kSiluThreads, 0, s, gate, ld_gate, up, ld_up, out, ld_out, rows, cols);
     }
     return launch_result("b2_silu_mul");
 }
@@ -486,10 +493,10 @@ int b2_moe_combine(const float* expert_out, size_t expert_rows, const uint8_t* r
     cudaStream_t s = as_stream(stream);
     if ((h % 4) == 0 && aligned16(expert_out) && aligned16(out)) {
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(moe_combine_rows<true>), kRowThreads, 0, T);
-        moe_combine_rows<true><<<grid, kRowThreads, 0, s>>>(expert_out, expert_rows, routes, route_positions, out, T, h);
+        launch_pdl(moe_combine_rows<true>, grid, kRowThreads, 0, s, expert_out, expert_rows, routes, route_positions, out, T, h);
     } else {
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(moe_combine_rows<false>), kRowThreads, 0, T);
-        moe_combine_rows<false><<<grid, kRowThreads, 0, s>>>(expert_out, expert_rows, routes, route_positions, out, T, h);
+        launch_pdl(moe_combine_rows<false>, grid, kRowThreads, 0, s, expert_out, expert_rows, routes, route_positions, out, T, h);
     }
     return launch_result("b2_moe_combine");
 }
@@ -502,10 +509,10 @@ int b2_add(float* a, const float* b, size_t n, b2_stream_t stream) {
     if ((n % 4) == 0 && aligned16(a) && aligned16(b)) {
         const std::size_t n4 = n / 4;
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(add_vec), 256, 0, (n4 + 511) / 512);
-        add_vec<<<grid, 256, 0, s>>>(reinterpret_cast<float4*>(a), reinterpret_cast<const float4*>(b), n4);
+        launch_pdl(add_vec, grid, 256, 0, s, reinterpret_cast<float4*>(a), reinterpret_cast<const float4*>(b), n4);
     } else {
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(add_scalar), 256, 0, (n + 255) / 256);
-        add_scalar<<<grid, 256, 0, s>>>(a, b, n);
+        launch_pdl(add_scalar, grid, 256, 0, s, a, b, n);
     }
     return launch_result("b2_add");
 }

@@ -44,6 +44,7 @@ struct RopeArgs {
 // Vector path: head_dim % 8 == 0 and 16-byte aligned operands.
 __global__ void __launch_bounds__(1024)
 rope_vec(RopeArgs a) {
+    pdl_begin();
     const unsigned half4 = static_cast<unsigned>(a.head_dim / 8);  // float4 per half head
     const unsigned per_row = static_cast<unsigned>(a.q_heads + a.kv_heads) * half4;
     const unsigned q_items = static_cast<unsigned>(a.q_heads) * half4;
@@ -101,6 +102,7 @@ rope_vec(RopeArgs a) {
 // Any even head_dim / alignment: one pair per thread, rows strided by CTA.
 __global__ void __launch_bounds__(256)
 rope_scalar(RopeArgs a) {
+    pdl_begin();
     const std::size_t half = a.head_dim / 2;
     const std::size_t per_row = (a.q_heads + a.kv_heads) * half;
     const std::size_t q_items = a.q_heads * half;
@@ -169,10 +171,10 @@ int b2_rope(float* q, float* k, const uint32_t* row_pos, size_t rows, size_t q_h
         if (threads > 1024) threads = 1024;
         const std::size_t steps = (rows + kRopeRowsPerStep - 1) / kRopeRowsPerStep;
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(rope_vec), threads, 0, steps);
-        rope_vec<<<grid, threads, 0, s>>>(a);
+        launch_pdl(rope_vec, grid, threads, 0, s, a);
     } else {
         const unsigned grid = wave_grid(reinterpret_cast<const void*>(rope_scalar), 256, 0, rows);
-        rope_scalar<<<grid, 256, 0, s>>>(a);
+        launch_pdl(rope_scalar, grid, 256, 0, s, a);
     }
     return launch_result("b2_rope");
 }

@@ -55,6 +55,7 @@ __device__ __forceinline__ float div_by_row(float e, float d, float y) {
 template <int THREADS, int V, bool EXACT>
 __global__ void __launch_bounds__(THREADS)
 causal_softmax_block(SoftmaxArgs a) {
+    pdl_begin();
     constexpr int WARPS = THREADS / 32;
     __shared__ float red[2][WARPS];
     __shared__ float denom_s;
@@ -145,6 +146,7 @@ constexpr int kWarpRowWarps = kWarpRowThreads / 32;
 template <int V, bool EXACT>
 __global__ void __launch_bounds__(kWarpRowThreads)
 causal_softmax_warp(SoftmaxArgs a) {
+    pdl_begin();
     __shared__ double tab[64];
     extern __shared__ __align__(16) float staged[];  // EXACT: kWarpRowWarps x T floats
     load_exp2_table(tab);
@@ -223,6 +225,7 @@ causal_softmax_warp(SoftmaxArgs a) {
 template <bool EXACT>
 __global__ void __launch_bounds__(kSmThreads)
 causal_softmax_smem(SoftmaxArgs a) {
+    pdl_begin();
     __shared__ float red[2][kSmWarps];
     __shared__ float denom_s;
     __shared__ double tab[64];
@@ -274,7 +277,7 @@ int launch_block(const SoftmaxArgs& a, cudaStream_t s) {
     if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("causal softmax: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), THREADS, smem, a.rows);
-    kernel<<<grid, THREADS, smem, s>>>(a);
+    launch_pdl(kernel, grid, THREADS, smem, s, a);
     return B2_OK;
 }
 
@@ -286,7 +289,7 @@ int launch_warp(const SoftmaxArgs& a, cudaStream_t s) {
         return launch_result("causal softmax: shared memory attribute");
     const std::size_t blocks = (a.rows + kWarpRowWarps - 1) / kWarpRowWarps;
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), kWarpRowThreads, smem, blocks);
-    kernel<<<grid, kWarpRowThreads, smem, s>>>(a);
+    launch_pdl(kernel, grid, kWarpRowThreads, smem, s, a);
     return B2_OK;
 }
 
@@ -297,7 +300,7 @@ int launch_smem(const SoftmaxArgs& a, cudaStream_t s) {
     if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("causal softmax: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), kSmThreads, smem, a.rows);
-    kernel<<<grid, kSmThreads, smem, s>>>(a);
+    launch_pdl(kernel, grid, kSmThreads, smem, s, a);
     return B2_OK;
 }
 

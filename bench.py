@@ -55,6 +55,10 @@ def parse():
     p.add_argument("--pool", type=int, default=0, help="stand-in sets (0 = fit to memory)")
     p.add_argument("--chunks", type=int, default=0, help="sub-batches per rank (0 = 1 on one GPU, 2 otherwise)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-kernel-timing", action="store_true",
+                   help="no per-launch events in the timed region (diagnostic; the line then lacks kernels/roofline)")
+    p.add_argument("--config", type=int, default=5, choices=[1, 2, 3, 4, 5],
+                   help="BASELINE config; 5 (default) is the headline, 1-4 single-GPU op chains")
     return p.parse_args()
 
 
@@ -195,6 +199,8 @@ def run_ours(args):
     if dist:
         dist.barrier()
     timers = [[StageTimer(args.layers) for _ in runner.pipes] for _ in range(args.steps)]
+    if args.no_kernel_timing:
+        timers = [None] * args.steps
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
@@ -218,7 +224,7 @@ def run_ours(args):
     bpr = prefill.bytes_per_row(args.layers)
     acc = {}
     for step_timers in timers:
-        for c, tm in enumerate(step_timers):
+        for c, tm in enumerate(step_timers or []):
             rows_c = runner.batches[c].rows
             for kind, vals in tm.durations().items():
                 a = acc.setdefault(kind, [0, 0.0, 0.0])
@@ -228,7 +234,7 @@ def run_ours(args):
     kern = {kind: dict(launches_per_step=n // args.steps, ms_per_step=round(t / args.steps, 4),
                        us_per_launch=round(t / n * 1e3, 2), gbs=round(b / (t * 1e-3) / 1e9, 1))
             for kind, (n, t, b) in acc.items()}
-    dominant = max(kern, key=lambda k: kern[k]["ms_per_step"])
+    dominant = max(kern, key=lambda k: kern[k]["ms_per_step"]) if kern else None
 
     # e2e: host ids -> tries -> H2D -> layers -> gather -> D2H of last-token rows
     last = torch.empty((args.prompts, prefill.HIDDEN), device=dev)
@@ -272,7 +278,7 @@ def run_ours(args):
     result = None
     if rank == 0:
         peak, peak_kind = peaks()
-        d = kern[dominant]
+        d = kern[dominant] if dominant else {"gbs": None}
         traffic = (round(TRAFFIC_BYTES_PER_ROW[dominant] * rows / len(runner.pipes))
                    if dominant in TRAFFIC_BYTES_PER_ROW else None)
         reasons = sorted(set(r for c in allclk for r in c.get("reasons", [])))
@@ -301,8 +307,8 @@ def run_ours(args):
                                                                   if world > 1 else "")},
             "hbm_gbs_algorithmic": round(bpr["total"] * rows * world / (ms_per_step / 1e3) / 1e9, 1),
             "roofline": {"kernel": dominant, "bound": "hbm", "achieved": d["gbs"], "peak": peak,
-                         "unit": "GB/s", "frac": round(d["gbs"] / peak, 3), "peak_kind": peak_kind,
-                         "traffic": traffic},
+                         "unit": "GB/s", "frac": round(d["gbs"] / peak, 3) if d["gbs"] else None,
+                         "peak_kind": peak_kind, "traffic": traffic},
             "kernels": kern,
             "clocks": {"sm_mhz": statistics.median(mhz) if mhz else None,
                        "sm_max_mhz": allclk[0].get("sm_max_mhz"), "reasons": reasons},
@@ -316,6 +322,102 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+# ---- single-GPU op chains: BASELINE configs 1-4 ----------------------------------------------
+
+
+def run_config(args) -> dict:
+    """Configs 1-4 on one GPU, each step one pass of the config's op chain,
+    L2 flushed (256 MB written) before every timed step, CUDA events around
+    the chain only. Value: algorithmic GB/s (config 4: tokens/s, GB/s in
+    roofline)."""
+    import math
+
+    import torch
+
+    from aps2026_b200 import ops, prefill
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(args.config - 1)
+    rn = lambda *s, std=1.0, mean=0.0: prefill._randn(s, gen, dev, mean, std)  # noqa: E731
+    flush = torch.empty(64 << 20, device=dev)
+    cfg = args.config
+    if cfg == 1:
+        x, y = rn(512, 4096), torch.empty(512, 4096, device=dev)
+        w, b = rn(4096, mean=1.0, std=0.1), rn(4096, std=0.1)
+        q, k = rn(512, 32 * 128), rn(512, 8 * 128)
+        pos = torch.arange(512, dtype=torch.int32, device=dev)
+        cos, sin = ops.rope_table_gpu(512, 128, 1e4, dev)
+
+        def chain():
+            ops.layer_norm_gpu(x, w, b, 1e-5, y, exact=args.exact)
+            ops.apply_rope_tree_gpu(q, k, pos, 512, 512, 32, 8, 128, 1e4)
+        nbytes, work = 38_043_648, "config 1: LayerNorm X[512,4096] + RoPE Q[512,32,128], K[512,8,128]"
+        tokens = 512
+    elif cfg == 2:
+        H, T = 32, 2048
+        scores, probs = rn(H, T, T, std=2.0), torch.empty(H, T, T, device=dev)
+        scale = float(np.float32(1.0) / np.sqrt(np.float32(128.0)))
+
+        def chain():
+            ops.causal_softmax_gpu(scores, probs, scale, 2047, exact=args.exact)
+        cells = sum(min(i + 1, 2047) for i in range(T))
+        nbytes = H * cells * 4 + H * T * T * 4
+        work, tokens = "config 2: causal scaled softmax [32, 2048, 2048], window 2047", H * T
+    elif cfg == 3:
+        T = 8192
+        logits = rn(T, 16)
+        gu, act = rn(2 * T, 896), torch.empty(2 * T, 448, device=dev)
+        eo, out = rn(2 * T, 4096), torch.empty(T, 4096, device=dev)
+        routing, ws = ops.alloc_routing(T, 16, dev), ops.RouteWorkspace(T, 16, dev)
+
+        def chain():
+            ops.moe_route_gpu(logits, routing, ws)
+            ops.silu_mul_gpu(gu[:, :448], gu[:, 448:], act)
+            ops.moe_combine_gpu(eo, routing.routes, routing.route_positions, out)
+        nbytes = (T * 16 * 4 + T * 2 + 2 * T * 4 * 2) + 2 * T * 448 * 12 + (2 * T * 4096 * 4 + T * 4096 * 4 + T * 10)
+        work, tokens = "config 3: top-2 routing T=8192 + SiLU [16384, 2x448] + un-permute to [8192, 4096]", T
+    else:
+        prompts = prefill.prompts_config4()
+        w = prefill.Weights.make(dev, 3, layers=1)
+        batch = prefill.Batch.build(prompts, dev)
+        sets = [prefill.StandIns.make(batch.rows, dev, gen)]
+        pipe = prefill.Pipeline(batch, w, dev, exact=args.exact)
+        pipe.bind_layers(sets, 1)
+
+        def chain():
+            pipe.run()
+        bpr = prefill.bytes_per_row(1)
+        nbytes = bpr["total"] * batch.rows
+        work = (f"config 4: one layer's non-GEMM path, 16 prompts x 1024 tokens with a 256-token shared prefix "
+                f"({batch.rows} trie rows)")
+        tokens = batch.tokens
+    for _ in range(args.warmup):
+        chain()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(0) as clocks:
+        for a, b_ in ev:
+            flush.zero_()
+            a.record()
+            chain()
+            b_.record()
+        torch.cuda.synchronize()
+    ms = statistics.median(a.elapsed_time(b_) for a, b_ in ev)
+    peak, peak_kind = peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    res = {"metric": f"config {cfg} " + ("non-GEMM tokens/s" if cfg == 4 else "algorithmic HBM GB/s"),
+           "value": round(tokens / (ms * 1e-3), 1) if cfg == 4 else round(gbs, 1),
+           "unit": "tokens/s" if cfg == 4 else "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "f32", "data": "synthetic (seeded)",
+           "config": {"workload": work, "algorithmic_bytes": nbytes, "exact_order": args.exact,
+                      "l2": "flushed (256 MB written) before every timed step"},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 3), "peak_kind": peak_kind, "traffic": None},
+           "clocks": {k: v for k, v in clocks.summary().items() if k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+    return res
 
 
 # ---- CPU baseline / reference arm ---------------------------------------------------------
@@ -454,6 +556,9 @@ def main():
         res = run_reference(args)
         if res is not None:
             print(json.dumps(res))
+        return
+    if args.config != 5:
+        print(json.dumps(run_config(args)))
         return
     res = run_ours(args)
     if res is not None:
