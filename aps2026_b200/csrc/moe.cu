@@ -23,6 +23,9 @@
 //      all CTAs together write the two work queues.
 // Token order within an expert is ascending, exactly what
 // k_moe_fill_stable produces; all integer outputs are bit-identical.
+#include <mutex>
+#include <string>
+
 #include "fastexp.cuh"
 #include "rowload.cuh"
 
@@ -518,3 +521,87 @@ int b2_add(float* a, const float* b, size_t n, b2_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---- routing for callers that cannot allocate device memory -----------------
+//
+// b2_moe_route takes its scratch (the per-tile expert histograms that pass
+// from the selection kernel to the scatter kernel) from the caller. Some
+// callers have no way to provide it: a plugin run by a host framework that
+// owns every device allocation and forbids allocating on its execution path,
+// or code that must not call cudaMalloc because it can synchronize the
+// device. b2_moe_route_noalloc runs the same two kernels with that scratch in
+// a fixed array compiled into this library instead.
+
+namespace b2 {
+namespace {
+
+// Fixed scratch of b2_moe_route_noalloc: 32768 words (128 KB), one histogram
+// row of padded_experts(E) words per 256-token tile. Every GPU that loads the
+// library holds it until the process exits.
+constexpr std::size_t kNoAllocScratchWords = 32768;
+static __device__ __align__(256) std::uint32_t g_route_scratch[kNoAllocScratchWords];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+std::uint32_t* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_route_scratch on the current device, looked up once
+// per device (in host code the array's name is not a device address).
+int route_scratch_address(std::uint32_t** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return set_error(B2_ERR_CUDA, std::string("b2_moe_route_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return set_error(B2_ERR_UNSUPPORTED, "b2_moe_route_noalloc: device index");
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_route_scratch);
+        if (e != cudaSuccess)
+            return set_error(B2_ERR_CUDA,
+                             std::string("b2_moe_route_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_scratch_addr[dev] = static_cast<std::uint32_t*>(p);
+    }
+    *out = g_scratch_addr[dev];
+    return B2_OK;
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" int b2_moe_route_noalloc(const float* logits, size_t T, size_t E, float quantum, float tie_eps,
+                                    uint8_t* routes, uint32_t* counts, uint32_t* offsets,
+                                    uint32_t* assignment_rows, uint32_t* route_positions,
+                                    uint32_t* work_expert64, uint32_t* work_start64, uint32_t* work_expert128,
+                                    uint32_t* work_start128, b2_stream_t stream) {
+    using namespace b2;
+    if (E < 2 || E > static_cast<size_t>(kMaxExperts))
+        return invalid("b2_moe_route_noalloc: E must be in [2, 32]");
+    if (T == 0) return B2_OK;
+    if (!logits || !routes || !counts || !offsets || !assignment_rows || !route_positions)
+        return invalid("b2_moe_route_noalloc: null pointer");
+    if ((reinterpret_cast<std::uintptr_t>(routes) & 1u) || (reinterpret_cast<std::uintptr_t>(route_positions) & 7u))
+        return invalid("b2_moe_route_noalloc: misaligned routes / route_positions");
+    const std::size_t tiles = route_tiles(T), ep = padded_experts(E);
+    if (tiles * ep > kNoAllocScratchWords)
+        return set_error(B2_ERR_UNSUPPORTED,
+                         "b2_moe_route_noalloc: T = " + std::to_string(T) + " with E = " + std::to_string(E) +
+                             " needs " + std::to_string(tiles * ep) + " scratch words, the fixed scratch holds " +
+                             std::to_string(kNoAllocScratchWords) + " (at most " +
+                             std::to_string(kNoAllocScratchWords / ep * kTile) +
+                             " tokens for this E); use b2_moe_route with a caller workspace");
+    std::uint32_t* scratch = nullptr;
+    if (int rc = route_scratch_address(&scratch)) return rc;
+    RouteArgs a{};
+    a.logits = logits; a.T = T; a.E = E; a.quantum = quantum; a.tie_eps = tie_eps;
+    a.routes = routes; a.counts = counts; a.offsets = offsets;
+    a.assignment_rows = assignment_rows; a.route_positions = route_positions;
+    a.we64 = work_expert64; a.ws64 = work_start64; a.we128 = work_expert128; a.ws128 = work_start128;
+    a.EP = static_cast<unsigned>(ep);
+    a.tile_counts = scratch;
+    a.tiles = tiles;
+    cudaStream_t s = as_stream(stream);
+    launch_pdl(route_select, static_cast<unsigned>(a.tiles), kTile, 0, s, a);
+    launch_pdl(route_scatter, static_cast<unsigned>(a.tiles), kTile, 0, s, a);
+    return launch_result("b2_moe_route_noalloc");
+}

@@ -200,6 +200,30 @@ int b2_moe_route(const float* logits, size_t T, size_t E, float quantum,
                  uint32_t* work_start128, void* workspace,
                  size_t workspace_bytes, b2_stream_t stream);
 
+/*
+ * b2_moe_route without a caller workspace -- no counterpart in the
+ * reference. For callers that cannot allocate device memory (a plugin whose
+ * host framework owns all device allocations and forbids allocating on its
+ * execution path, or code that must not call cudaMalloc because it can
+ * synchronize the device). Same arguments and outputs as b2_moe_route minus
+ * the workspace; allocates nothing: the per-tile histograms live in a fixed
+ * 128 KB array compiled into the library (held by every GPU that loads it
+ * until the process exits), which limits ceil(T/256) * E' to 32768 words
+ * with E' = E rounded up to a power of two >= 4 (524,288 tokens at E = 16);
+ * larger requests return B2_ERR_UNSUPPORTED. The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture. All calls on a device share the array: calls
+ * that overlap on the GPU (other streams, other host threads) race on it.
+ * Every word a call reads it has written first, so nothing needs clearing.
+ */
+int b2_moe_route_noalloc(const float* logits, size_t T, size_t E,
+                         float quantum, float tie_eps, uint8_t* routes,
+                         uint32_t* counts, uint32_t* offsets,
+                         uint32_t* assignment_rows,
+                         uint32_t* route_positions, uint32_t* work_expert64,
+                         uint32_t* work_start64, uint32_t* work_expert128,
+                         uint32_t* work_start128, b2_stream_t stream);
+
 /* ---- expert activation, un-permute, residual ------------------------------ */
 
 /*
