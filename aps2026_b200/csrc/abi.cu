@@ -51,6 +51,7 @@ int take_check_gather(cudaStream_t, unsigned int*);
 int take_check_layernorm(cudaStream_t, unsigned int*);
 int take_check_rope(cudaStream_t, unsigned int*);
 int take_check_moe(cudaStream_t, unsigned int*);
+int take_check_attention(cudaStream_t, unsigned int*);
 
 }  // namespace b2
 
@@ -69,6 +70,7 @@ int b2_device_status(uint32_t* status_out, b2_stream_t stream) {
     if ((rc = b2::take_check_layernorm(s, &acc)) != B2_OK) return rc;
     if ((rc = b2::take_check_rope(s, &acc)) != B2_OK) return rc;
     if ((rc = b2::take_check_moe(s, &acc)) != B2_OK) return rc;
+    if ((rc = b2::take_check_attention(s, &acc)) != B2_OK) return rc;
     *status_out = acc;
     return B2_OK;
 }

@@ -71,7 +71,7 @@ int b2_prefill_layers(const b2_prefill_shape* shape, const float* emb, size_t vo
     cudaStream_t cs = as_stream(stream);
     // Optional timing: event pair i brackets launch i (layout in the header).
     auto mark = [&](size_t pair, int end) -> int {
-        if (!events) return B2_OK;
+        if (!events || !events[2 * pair + end]) return B2_OK;
         const cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(events[2 * pair + end]), cs);
         return e == cudaSuccess ? B2_OK : set_error(B2_ERR_CUDA, std::string("event record: ") + cudaGetErrorString(e));
     };

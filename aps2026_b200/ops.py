@@ -204,6 +204,21 @@ def causal_softmax_gpu(scores, probs, scale: float, window: int = SLIDING_WINDOW
                                         _flags(exact), _stream()), "causal_softmax_gpu")
 
 
+def attention_tree_gpu(q, k, v, out, row_pos, anc, anc_stride: int, rows: int, q_heads: int, kv_heads: int,
+                       head_dim: int, window: int = SLIDING_WINDOW, exact: bool = False) -> None:
+    """Prefix-tree GQA-4 attention on trie rows (tensor_ops::attention_tree_gpu,
+    include/tensor.h:109-114); anc: device int32 [rows, anc_stride]."""
+    if q_heads != 4 * kv_heads:
+        raise InvalidArgument("attention_tree_gpu expects GQA-4")
+    if (q.numel() != rows * q_heads * head_dim or out.numel() != q.numel()
+            or k.numel() != rows * kv_heads * head_dim or v.numel() != k.numel()
+            or row_pos.numel() != rows or anc.numel() != rows * anc_stride):
+        raise InvalidArgument("attention shape")
+    _check(_lib.lib().b2_attention_tree(_f32(q), _f32(k), _f32(v), _f32(out), _u32(row_pos), _u32(anc), anc_stride,
+                                        rows, q_heads, kv_heads, head_dim, window, _flags(exact), _stream()),
+           "attention_tree_gpu")
+
+
 # ---- MoE ----------------------------------------------------------------------------------
 
 

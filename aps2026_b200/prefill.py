@@ -345,13 +345,30 @@ class StageTimer:
 
     STAGES = ("rope", "add_ln", "route", "silu")
 
-    def __init__(self, layers: int):
+    def __init__(self, layers: int, kinds=None):
+        """`kinds` (default: all) limits the records to those launch kinds
+        ('ln0', 'fused', 'rope', 'add_ln', 'route', 'silu'): an event
+        between two launches also serialises them, so fewer records
+        disturb the run less."""
         self.layers = layers
+        self.kinds = set(kinds) if kinds is not None else {"ln0", "fused", *self.STAGES}
         self.events = [torch.cuda.Event(enable_timing=True) for _ in range(2 * (5 * layers + 1))]
         for e in self.events:  # materialise the driver events
             e.record()
         torch.cuda.synchronize()
-        self._arr = (C.c_void_p * len(self.events))(*[e.cuda_event for e in self.events])
+        handles = [e.cuda_event for e in self.events]
+        for pair in range(5 * layers + 1):
+            if self._kind(pair) not in self.kinds:
+                handles[2 * pair] = handles[2 * pair + 1] = None
+        self._arr = (C.c_void_p * len(self.events))(*handles)
+
+    def _kind(self, pair: int) -> str:
+        L = self.layers
+        if pair == 0:
+            return "ln0"
+        if pair <= L:
+            return "fused"
+        return self.STAGES[(pair - L - 1) % 4]
 
     def handles(self):
         return self._arr
@@ -360,13 +377,14 @@ class StageTimer:
         return self.events[2 * pair].elapsed_time(self.events[2 * pair + 1])
 
     def durations(self) -> dict:
-        """ms per launch kind after the run has completed: 'ln0', 'fused'
-        (layers 1..L-1 and the final step), and the four per-layer stages."""
+        """ms per launch of each recorded kind after the run has completed:
+        'ln0', 'fused' (layers 1..L-1 and the final step), and the four
+        per-layer stages."""
         L = self.layers
         out = {"ln0": [self._ms(0)], "fused": [self._ms(l) for l in range(1, L + 1)]}
         for s, name in enumerate(self.STAGES):
             out[name] = [self._ms(L + 1 + 4 * l + s) for l in range(L)]
-        return out
+        return {k: v for k, v in out.items() if k in self.kinds}
 
 
 # ---- algorithmic bytes (per trie-node row) ----------------------------------------------------

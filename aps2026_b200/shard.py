@@ -31,14 +31,47 @@ def shard_prompts(prompts: Sequence[Sequence[int]], world: int) -> list[list[int
     return [sorted(x) for x in out]
 
 
-def chunk_plan(prompts: Sequence[Sequence[int]], world: int, chunks: int) -> list[list[list[int]]]:
+def split_by_fraction(prompts: Sequence[Sequence[int]], idx: Sequence[int],
+                      fractions: Sequence[float]) -> list[list[int]]:
+    """Splits the prompts `idx` (kept in order, prompts that share a first
+    token kept together) into consecutive parts holding about `fractions`
+    of their tokens."""
+    groups: dict[int, list[int]] = {}
+    for i in idx:
+        groups.setdefault(int(prompts[i][0]) if len(prompts[i]) else -1, []).append(i)
+    total = sum(len(prompts[i]) for i in idx)
+    targets = [f * total for f in fractions]
+    parts: list[list[int]] = [[] for _ in fractions]
+    c, filled = 0, 0.0
+    for g in groups.values():
+        size = sum(len(prompts[i]) for i in g)
+        while c < len(parts) - 1 and filled >= targets[c] - 1e-9:
+            c, filled = c + 1, 0.0
+        parts[c].extend(g)
+        filled += size
+    return [sorted(p) for p in parts]
+
+
+def chunk_plan(prompts: Sequence[Sequence[int]], world: int, chunks: int,
+               fractions: Sequence[float] | None = None) -> list[list[list[int]]]:
     """plan[rank][chunk] = global prompt indices: the rank shards of
-    shard_prompts, each split again into `chunks` sub-batches the same way
-    (empty sub-batches dropped)."""
+    shard_prompts, each split again into `chunks` sub-batches -- balanced,
+    or holding `fractions` of the rank's tokens in order (a large first
+    chunk hides the gather of the earlier chunks behind the later ones);
+    empty sub-batches dropped."""
     plan = []
     for mine in shard_prompts(prompts, world):
-        sub = shard_prompts([prompts[i] for i in mine], chunks) if mine else []
-        plan.append([[mine[j] for j in part] for part in sub if part])
+        if not mine:
+            plan.append([])
+            continue
+        if fractions is not None:
+            if len(fractions) != chunks:
+                raise ValueError("one fraction per chunk")
+            sub = split_by_fraction(prompts, mine, fractions)
+            plan.append([p for p in sub if p])
+        else:
+            sub = shard_prompts([prompts[i] for i in mine], chunks)
+            plan.append([[mine[j] for j in part] for part in sub if part])
     return plan
 
 

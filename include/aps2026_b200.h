@@ -166,6 +166,26 @@ int b2_causal_softmax(const float* scores, float* probs, size_t heads,
                       size_t T, size_t ld, float scale, size_t window,
                       uint32_t flags, b2_stream_t stream);
 
+/*
+ * Prefix-tree GQA attention core: for trie row r and KV head h, the keys
+ * and values are the rows of r's ancestor chain anc[r * anc_stride + begin
+ * .. + pos] (pos = row_pos[r], begin = max(0, pos + 1 - window)); each of
+ * the 4 query heads of h gets softmax(q . k * 1/sqrt(head_dim)) . v.
+ * q, out: [rows, q_heads*head_dim]; k, v: [rows, kv_heads*head_dim];
+ * q_heads = 4 * kv_heads; head_dim 64 or 128. Same arithmetic and order as
+ * k_attention_tree_gqa4 (src/tensor.cu:2425-2633; wrapper
+ * tensor_ops::attention_tree_gpu, include/tensor.h:109-114, :3361-3377;
+ * the reference's window is SLIDING_WINDOW = 2047): bit-identical with
+ * B2_FLAG_EXACT_ORDER, within tolerance with tree-order softmax sums.
+ * A row whose position is >= anc_stride, or a chain entry >= rows, is
+ * reported through b2_device_status (B2_CHECK_ATTENTION).
+ */
+int b2_attention_tree(const float* q, const float* k, const float* v,
+                      float* out, const uint32_t* row_pos,
+                      const uint32_t* anc, size_t anc_stride, size_t rows,
+                      size_t q_heads, size_t kv_heads, size_t head_dim,
+                      size_t window, uint32_t flags, b2_stream_t stream);
+
 /* ---- MoE routing (bit-exact) ---------------------------------------------- */
 
 /* Bytes of caller workspace b2_moe_route needs for T tokens, E experts. */
@@ -362,7 +382,8 @@ typedef struct b2_prefill_work {
  * [2i, 2i+1]: i = l < num_layers is layer l's LN1 step (plain LN for l = 0,
  * the fused un-permute + add + LN otherwise), i = num_layers the final fused
  * step, i = num_layers + 1 + 4l + s layer l's RoPE (s = 0), add + LN2 (1),
- * routing (2) and SiLU (3). Kernel launches issued: B2_PREFILL_LAUNCHES(L).
+ * routing (2) and SiLU (3); a NULL handle in the array skips that record.
+ * Kernel launches issued: B2_PREFILL_LAUNCHES(L).
  */
 #define B2_PREFILL_LAUNCHES(num_layers) (2 + 6 * (num_layers))
 int b2_prefill_layers(const b2_prefill_shape* shape, const float* emb, size_t vocab,

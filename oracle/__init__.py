@@ -60,6 +60,7 @@ def lib() -> C.CDLL:
             "orc_moe_combine_add_layer_norm": (None, [_vp] * 8 + [_sz, _sz, _f32]),
             "orc_add": (None, [_vp, _vp, _sz]),
             "orc_prefix_trie": (C.c_longlong, [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp, _sz]),
+            "orc_attention_tree": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(h, name)
@@ -174,6 +175,17 @@ def moe_route(logits, quantum=1e-3, tie_eps=2e-2):
     lib().orc_moe_route(_p(logits), T, E, quantum, tie_eps, *[_p(out[k]) for k in (
         "routes", "counts", "offsets", "assignment_rows", "route_positions", "work_expert64",
         "work_start64", "work_expert128", "work_start128")])
+    return out
+
+
+def attention_tree(q, k, v, row_pos, anc, q_heads, kv_heads, head_dim, window):
+    """Prefix-tree GQA attention of k_attention_tree_gqa4; anc is
+    [rows, anc_stride]."""
+    q, k, v, row_pos, anc = f32(q), f32(k), f32(v), u32(row_pos), u32(anc)
+    rows = row_pos.size
+    out = np.empty((rows, q_heads * head_dim), np.float32)
+    lib().orc_attention_tree(_p(q), _p(k), _p(v), _p(out), _p(row_pos), _p(anc), anc.shape[1], rows, q_heads,
+                             kv_heads, head_dim, window)
     return out
 
 

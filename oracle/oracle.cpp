@@ -273,6 +273,70 @@ void orc_moe_route(const float* logits, std::size_t T, std::size_t E,
         }
 }
 
+// k_attention_tree_gqa4 (src/tensor.cu:2425-2633): per (row, kv head), the
+// keys are the row's ancestor chain [begin, pos] (begin = pos + 1 - window
+// when positive, :2435-2439); for each of the `group` query heads the score
+// of key w is the 128-wide dot product in four accumulators over d mod 4,
+// each a fused multiply-add chain in ascending d (:2517-2524), combined as
+// (acc0 + acc1) + (acc2 + acc3), times 1/sqrtf(head_dim) (:2448, :2526);
+// then the softmax of orc_causal_softmax (max, (float)exp((double)(s-max)),
+// serial ascending denominator, division, :2549-2585); then
+// out[d] = fma chain of p[w] * v[chain[w]][d] in ascending w (:2596-2631).
+void orc_attention_tree(const float* q, const float* k, const float* v, float* out,
+                        const std::uint32_t* row_pos, const std::uint32_t* anc,
+                        std::size_t anc_stride, std::size_t rows, std::size_t q_heads,
+                        std::size_t kv_heads, std::size_t head_dim, std::size_t window) {
+    const std::size_t group = q_heads / kv_heads;
+    const float scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
+#pragma omp parallel
+    {
+        std::vector<float> sc;
+#pragma omp for schedule(dynamic, 8)
+        for (long long task = 0; task < static_cast<long long>(rows * kv_heads); ++task) {
+            const std::size_t row = static_cast<std::size_t>(task) / kv_heads;
+            const std::size_t kh = static_cast<std::size_t>(task) % kv_heads;
+            const std::size_t pos = row_pos[row];
+            const std::size_t begin = pos + 1 > window ? pos + 1 - window : 0;
+            const std::size_t W = pos - begin + 1;
+            const std::uint32_t* chain = anc + row * anc_stride + begin;
+            sc.resize(W);
+            for (std::size_t g = 0; g < group; ++g) {
+                const float* qv = q + (row * q_heads + kh * group + g) * head_dim;
+                for (std::size_t w = 0; w < W; ++w) {
+                    const float* kv = k + (static_cast<std::size_t>(chain[w]) * kv_heads + kh) * head_dim;
+                    float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
+                    std::size_t d = 0;
+                    for (; d + 4 <= head_dim; d += 4) {
+                        acc0 = std::fma(qv[d + 0], kv[d + 0], acc0);
+                        acc1 = std::fma(qv[d + 1], kv[d + 1], acc1);
+                        acc2 = std::fma(qv[d + 2], kv[d + 2], acc2);
+                        acc3 = std::fma(qv[d + 3], kv[d + 3], acc3);
+                    }
+                    float score = (acc0 + acc1) + (acc2 + acc3);
+                    for (; d < head_dim; ++d) score = std::fma(qv[d], kv[d], score);
+                    sc[w] = score * scale;
+                }
+                float maxv = -3.402823466e+38F;
+                for (std::size_t w = 0; w < W; ++w) maxv = std::fmax(maxv, sc[w]);
+                float denom = 0.0f;
+                for (std::size_t w = 0; w < W; ++w) {
+                    sc[w] = static_cast<float>(std::exp(static_cast<double>(sc[w] - maxv)));
+                    denom += sc[w];
+                }
+                for (std::size_t w = 0; w < W; ++w) sc[w] = sc[w] / denom;
+                float* o = out + (row * q_heads + kh * group + g) * head_dim;
+                for (std::size_t dd = 0; dd < head_dim; ++dd) {
+                    float value = 0.0f;
+                    for (std::size_t w = 0; w < W; ++w)
+                        value = std::fma(sc[w], v[(static_cast<std::size_t>(chain[w]) * kv_heads + kh) * head_dim + dd],
+                                         value);
+                    o[dd] = value;
+                }
+            }
+        }
+    }
+}
+
 // k_silu_mul (src/tensor.cu:2001-2010) on strided rows.
 void orc_silu_mul(const float* gate, std::size_t ldg, const float* up,
                   std::size_t ldu, float* out, std::size_t ldo,

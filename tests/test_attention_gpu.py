@@ -1,0 +1,89 @@
+"""The prefix-tree attention core (b2_attention_tree) against the oracle's
+restatement of k_attention_tree_gqa4 and against that reference kernel
+itself (oracle/_ref), on trie rows of prompts with shared prefixes.
+B2_FLAG_EXACT_ORDER: bit-exact; tree-order softmax sums: north_star
+tolerance."""
+import numpy as np
+import pytest
+
+import oracle
+from tests._util import normal, rng, to_dev, to_host
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(seed, prompts, length, shared, q_heads=16, kv_heads=4, hd=128):
+    g = rng(seed)
+    base = g.integers(0, 500, shared)
+    ps = [np.concatenate([base, g.integers(0, 500, length - shared)]).astype(np.int32) for _ in range(prompts)]
+    t = oracle.prefix_trie(ps, vocab=500)
+    R = t["nodes"]
+    q = normal(g, (R, q_heads * hd))
+    k = normal(g, (R, kv_heads * hd))
+    v = normal(g, (R, kv_heads * hd))
+    return t, q, k, v
+
+
+@pytest.mark.parametrize("prompts,length,shared,window", [(3, 300, 40, 2047), (2, 700, 10, 100), (1, 5, 0, 2047)])
+@pytest.mark.parametrize("exact", [True, False])
+def test_attention_tree_vs_oracle(cuda, prompts, length, shared, window, exact):
+    import torch
+
+    from aps2026_b200 import ops
+
+    t, q, k, v = _case(50, prompts, length, shared)
+    R, stride = t["nodes"], t["node_anc"].shape[1]
+    want = oracle.attention_tree(q, k, v, t["node_depth"], t["node_anc"], 16, 4, 128, window)
+    out = torch.full((R, 16 * 128), float("nan"), device=cuda)
+    pos, anc = to_dev(t["node_depth"], cuda), to_dev(np.ascontiguousarray(t["node_anc"]), cuda)
+    ops.attention_tree_gpu(to_dev(q, cuda), to_dev(k, cuda), to_dev(v, cuda), out, pos, anc, stride, R, 16, 4, 128,
+                           window, exact=exact)
+    torch.cuda.synchronize()
+    if exact:
+        oracle.assert_bitexact(to_host(out), want, "attention exact")
+    else:
+        oracle.assert_close(to_host(out), want, what="attention")
+    assert ops.device_status() == 0
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref/libref.so not built")
+def test_attention_tree_vs_reference_kernel(cuda):
+    import torch
+
+    from aps2026_b200 import ops
+
+    t, q, k, v = _case(51, 4, 400, 64)
+    R, stride = t["nodes"], t["node_anc"].shape[1]
+    qd, kd, vd = to_dev(q, cuda), to_dev(k, cuda), to_dev(v, cuda)
+    pos, anc = to_dev(t["node_depth"], cuda), to_dev(np.ascontiguousarray(t["node_anc"]), cuda)
+    ref = torch.empty((R, 16 * 128), device=cuda)
+    st = torch.cuda.current_stream().cuda_stream
+    rc = oracle.ref().ref_k_attention_tree(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), ref.data_ptr(),
+                                           pos.data_ptr(), anc.data_ptr(), stride, R, stride, 16, 4, 128, st)
+    assert rc == 0
+    torch.cuda.synchronize()
+    want = oracle.attention_tree(q, k, v, t["node_depth"], t["node_anc"], 16, 4, 128, oracle.ref().ref_sliding_window())
+    oracle.assert_bitexact(want, to_host(ref), "oracle vs reference attention")
+    out = torch.empty_like(ref)
+    ops.attention_tree_gpu(qd, kd, vd, out, pos, anc, stride, R, 16, 4, 128, 2047, exact=True)
+    torch.cuda.synchronize()
+    oracle.assert_bitexact(to_host(out), to_host(ref), "b2 exact vs reference attention")
+
+
+def test_attention_tree_bad_index_is_reported(cuda):
+    import torch
+
+    from aps2026_b200 import ops
+
+    t, q, k, v = _case(52, 1, 20, 0)
+    R, stride = t["nodes"], t["node_anc"].shape[1]
+    anc = np.ascontiguousarray(t["node_anc"]).copy()
+    anc[5, 2] = R + 100                       # a chain entry outside the rows
+    depth = t["node_depth"].copy()
+    depth[7] = stride                          # a position outside the ancestor table
+    out = torch.empty((R, 16 * 128), device=cuda)
+    ops.attention_tree_gpu(to_dev(q, cuda), to_dev(k, cuda), to_dev(v, cuda), out, to_dev(depth, cuda),
+                           to_dev(anc, cuda), stride, R, 16, 4, 128, 2047)
+    status = ops.device_status()
+    assert status & 8
+    assert torch.equal(out[7], torch.zeros_like(out[7]))
