@@ -69,56 +69,65 @@ __device__ __forceinline__ float quantize(float s, float quantum) {
     return s < 0.0f ? -r : r;
 }
 
+// The two experts of token t, first | second << 8, as k_moe_top2 picks
+// them (src/tensor.cu:1299-1328): the first scan takes an expert when its
+// quantized score beats the best so far by more than tie_eps, the second
+// scan does the same skipping the first pick; also stored to routes[t].
+__device__ __forceinline__ unsigned pick_top2(const RouteArgs& a, std::size_t t) {
+    const unsigned E = static_cast<unsigned>(a.E);
+    float sc[kMaxExperts];
+    const float* row = a.logits + t * a.E;
+    if ((E & 3u) == 0 && aligned16(row)) {
+#pragma unroll
+        for (unsigned e = 0; e < kMaxExperts; e += 4)
+            if (e < E) {
+                const float4 v = ld_stream(reinterpret_cast<const float4*>(row + e));
+                sc[e] = v.x; sc[e + 1] = v.y; sc[e + 2] = v.z; sc[e + 3] = v.w;
+            }
+    } else {
+#pragma unroll
+        for (unsigned e = 0; e < kMaxExperts; ++e)
+            if (e < E) sc[e] = __ldg(row + e);
+    }
+    int first = -1;
+    float first_value = -3.402823466e+38F;
+#pragma unroll
+    for (unsigned e = 0; e < kMaxExperts; ++e)
+        if (e < E) {
+            sc[e] = quantize(sc[e], a.quantum);
+            if (first < 0 || sc[e] > __fadd_rn(first_value, a.tie_eps)) {
+                first = static_cast<int>(e);
+                first_value = sc[e];
+            }
+        }
+    int second = -1;
+    float second_value = -3.402823466e+38F;
+#pragma unroll
+    for (unsigned e = 0; e < kMaxExperts; ++e)
+        if (e < E && static_cast<int>(e) != first) {
+            if (second < 0 || sc[e] > __fadd_rn(second_value, a.tie_eps)) {
+                second = static_cast<int>(e);
+                second_value = sc[e];
+            }
+        }
+    const unsigned short pair =
+        static_cast<unsigned short>(first) | (static_cast<unsigned short>(second) << 8);
+    reinterpret_cast<unsigned short*>(a.routes)[t] = pair;
+    return pair;
+}
+
 __global__ void __launch_bounds__(kTile)
 route_select(RouteArgs a) {
     pdl_begin();
     __shared__ unsigned int hist[kMaxExperts];
-    const unsigned E = static_cast<unsigned>(a.E);
     if (threadIdx.x < kMaxExperts) hist[threadIdx.x] = 0;
     __syncthreads();
 
     const std::size_t t = static_cast<std::size_t>(blockIdx.x) * kTile + threadIdx.x;
     if (t < a.T) {
-        float sc[kMaxExperts];
-        const float* row = a.logits + t * a.E;
-        if ((E & 3u) == 0 && aligned16(row)) {
-#pragma unroll
-            for (unsigned e = 0; e < kMaxExperts; e += 4)
-                if (e < E) {
-                    const float4 v = ld_stream(reinterpret_cast<const float4*>(row + e));
-                    sc[e] = v.x; sc[e + 1] = v.y; sc[e + 2] = v.z; sc[e + 3] = v.w;
-                }
-        } else {
-#pragma unroll
-            for (unsigned e = 0; e < kMaxExperts; ++e)
-                if (e < E) sc[e] = __ldg(row + e);
-        }
-        int first = -1;
-        float first_value = -3.402823466e+38F;
-#pragma unroll
-        for (unsigned e = 0; e < kMaxExperts; ++e)
-            if (e < E) {
-                sc[e] = quantize(sc[e], a.quantum);
-                if (first < 0 || sc[e] > __fadd_rn(first_value, a.tie_eps)) {
-                    first = static_cast<int>(e);
-                    first_value = sc[e];
-                }
-            }
-        int second = -1;
-        float second_value = -3.402823466e+38F;
-#pragma unroll
-        for (unsigned e = 0; e < kMaxExperts; ++e)
-            if (e < E && static_cast<int>(e) != first) {
-                if (second < 0 || sc[e] > __fadd_rn(second_value, a.tie_eps)) {
-                    second = static_cast<int>(e);
-                    second_value = sc[e];
-                }
-            }
-        const unsigned short pair =
-            static_cast<unsigned short>(first) | (static_cast<unsigned short>(second) << 8);
-        reinterpret_cast<unsigned short*>(a.routes)[t] = pair;
-        atomicAdd(&hist[first], 1u);
-        atomicAdd(&hist[second], 1u);
+        const unsigned pair = pick_top2(a, t);
+        atomicAdd(&hist[pair & 0xFFu], 1u);
+        atomicAdd(&hist[pair >> 8], 1u);
     }
     __syncthreads();
     if (threadIdx.x < a.EP)
@@ -135,13 +144,96 @@ __device__ __forceinline__ uint4 shfl_xor_u4(const uint4& v, int o) {
                       __shfl_xor_sync(0xffffffffu, v.z, o), __shfl_xor_sync(0xffffffffu, v.w, o));
 }
 
+// Shared-memory results of the per-expert scan.
+struct ExpertScan {
+    unsigned offs[kMaxExperts + 1];  // offsets; [E] = 2T
+    unsigned q64[kMaxExperts + 1];   // first 64-row queue entry per expert; [E] = entries used
+    unsigned q128[kMaxExperts + 1];
+    unsigned base[kMaxExperts];      // offsets[e] + rows of expert e in earlier tokens
+};
+
+// Warp-wide (lane = expert): from each expert's total and its count in
+// tokens before this CTA's, the exclusive scans over experts -- offsets and
+// the bases of the two work queues -- into `sc`; `write_counts` also stores
+// counts/offsets (one CTA does).
+__device__ __forceinline__ void scan_experts(const RouteArgs& a, unsigned lane, unsigned tot, unsigned bef,
+                                             bool write_counts, ExpertScan& sc) {
+    const unsigned E = static_cast<unsigned>(a.E);
+    const unsigned e = lane;
+    unsigned incl = tot, c64 = (tot + 63) / 64, c128 = (tot + 127) / 128;
+    unsigned i64 = c64, i128 = c128;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
+        const unsigned n64 = __shfl_up_sync(0xffffffffu, i64, o);
+        const unsigned n128 = __shfl_up_sync(0xffffffffu, i128, o);
+        if (lane >= static_cast<unsigned>(o)) { incl += n; i64 += n64; i128 += n128; }
+    }
+    if (e < E) {
+        sc.offs[e] = incl - tot;
+        sc.q64[e] = i64 - c64;
+        sc.q128[e] = i128 - c128;
+        sc.base[e] = incl - tot + bef;
+    }
+    // lane 31's inclusive sums are the grand totals (lanes >= E add 0)
+    const unsigned all_rows = __shfl_sync(0xffffffffu, incl, 31);
+    const unsigned all64 = __shfl_sync(0xffffffffu, i64, 31);
+    const unsigned all128 = __shfl_sync(0xffffffffu, i128, 31);
+    if (lane == 0) {
+        sc.offs[E] = all_rows;
+        sc.q64[E] = all64;
+        sc.q128[E] = all128;
+    }
+    if (write_counts) {
+        if (e < E) {
+            a.counts[e] = tot;
+            a.offsets[e] = incl - tot;
+        }
+        if (lane == 0) a.offsets[E] = all_rows;
+    }
+}
+
+// Work queues, entries first, first + stride, ...: entry i belongs to the
+// expert whose chunk range holds it; entries past the last chunk are
+// 0xFFFFFFFF (the reference memsets the expert queues to 0xff; the start
+// queues get the same marker).
+__device__ __forceinline__ void fill_queues(const RouteArgs& a, const ExpertScan& sc, std::size_t first,
+                                            std::size_t stride) {
+    const unsigned E = static_cast<unsigned>(a.E);
+    const std::size_t n64 = (2 * a.T + 63) / 64 + a.E, n128 = (2 * a.T + 127) / 128 + a.E;
+    const std::size_t nq = n64 > n128 ? n64 : n128;
+    for (std::size_t i = first; i < nq; i += stride) {
+        if (i < n64) {
+            std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
+            if (i < sc.q64[E]) {
+                unsigned e = 0;
+                while (i >= sc.q64[e + 1]) ++e;
+                ex = e;
+                st = sc.offs[e] + static_cast<std::uint32_t>(i - sc.q64[e]) * 64u;
+            }
+            if (a.we64) a.we64[i] = ex;
+            if (a.ws64) a.ws64[i] = st;
+        }
+        if (i < n128) {
+            std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
+            if (i < sc.q128[E]) {
+                unsigned e = 0;
+                while (i >= sc.q128[e + 1]) ++e;
+                ex = e;
+                st = sc.offs[e] + static_cast<std::uint32_t>(i - sc.q128[e]) * 128u;
+            }
+            if (a.we128) a.we128[i] = ex;
+            if (a.ws128) a.ws128[i] = st;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kTile)
 route_scatter(RouteArgs a) {
     pdl_begin();
     constexpr int WARPS = kTile / 32;
     __shared__ uint4 red_all[WARPS][kMaxExperts / 4], red_before[WARPS][kMaxExperts / 4];
-    __shared__ unsigned int base_s[kMaxExperts], offs_s[kMaxExperts + 1];
-    __shared__ unsigned int q64_s[kMaxExperts + 1], q128_s[kMaxExperts + 1];
+    __shared__ ExpertScan sc;
     __shared__ unsigned int warp_cnt[WARPS][kMaxExperts];
     __shared__ unsigned int warp_base[WARPS][kMaxExperts];
     const unsigned E = static_cast<unsigned>(a.E);
@@ -179,38 +271,7 @@ route_scatter(RouteArgs a) {
                 bef += rb[w * (kMaxExperts) + e];
             }
         }
-        // exclusive scans over experts: offsets and the two queue bases
-        unsigned incl = tot, c64 = (tot + 63) / 64, c128 = (tot + 127) / 128;
-        unsigned i64 = c64, i128 = c128;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
-            const unsigned n64 = __shfl_up_sync(0xffffffffu, i64, o);
-            const unsigned n128 = __shfl_up_sync(0xffffffffu, i128, o);
-            if (lane >= static_cast<unsigned>(o)) { incl += n; i64 += n64; i128 += n128; }
-        }
-        if (e < E) {
-            offs_s[e] = incl - tot;
-            q64_s[e] = i64 - c64;
-            q128_s[e] = i128 - c128;
-            base_s[e] = incl - tot + bef;
-        }
-        // lane 31's inclusive sums are the grand totals (lanes >= E add 0)
-        const unsigned all_rows = __shfl_sync(0xffffffffu, incl, 31);
-        const unsigned all64 = __shfl_sync(0xffffffffu, i64, 31);
-        const unsigned all128 = __shfl_sync(0xffffffffu, i128, 31);
-        if (lane == 0) {
-            offs_s[E] = all_rows;
-            q64_s[E] = all64;
-            q128_s[E] = all128;
-        }
-        if (blockIdx.x == 0) {
-            if (e < E) {
-                a.counts[e] = tot;
-                a.offsets[e] = incl - tot;
-            }
-            if (lane == 0) a.offsets[E] = all_rows;
-        }
+        scan_experts(a, lane, tot, bef, blockIdx.x == 0, sc);
     }
 
     // ---- stable ranks inside the tile ----
@@ -231,7 +292,7 @@ route_scatter(RouteArgs a) {
     __syncthreads();
     if (threadIdx.x < E) {
         const unsigned e = threadIdx.x;
-        unsigned base = base_s[e];
+        unsigned base = sc.base[e];
         for (int w = 0; w < WARPS; ++w) {
             warp_base[w][e] = base;
             base += warp_cnt[w][e];
@@ -249,36 +310,8 @@ route_scatter(RouteArgs a) {
         reinterpret_cast<uint2*>(a.route_positions)[t] = make_uint2(p0, p1);
     }
 
-    // ---- work queues: entry i belongs to the expert whose chunk range holds
-    // it; entries past the last chunk are 0xFFFFFFFF (the reference memsets
-    // the expert queues to 0xff; the start queues get the same marker) ----
-    const std::size_t n64 = (2 * a.T + 63) / 64 + a.E, n128 = (2 * a.T + 127) / 128 + a.E;
-    const std::size_t nq = n64 > n128 ? n64 : n128;
-    for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * kTile + threadIdx.x; i < nq;
-         i += static_cast<std::size_t>(gridDim.x) * kTile) {
-        if (i < n64) {
-            std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
-            if (i < q64_s[E]) {
-                unsigned e = 0;
-                while (i >= q64_s[e + 1]) ++e;
-                ex = e;
-                st = offs_s[e] + static_cast<std::uint32_t>(i - q64_s[e]) * 64u;
-            }
-            if (a.we64) a.we64[i] = ex;
-            if (a.ws64) a.ws64[i] = st;
-        }
-        if (i < n128) {
-            std::uint32_t ex = 0xFFFFFFFFu, st = 0xFFFFFFFFu;
-            if (i < q128_s[E]) {
-                unsigned e = 0;
-                while (i >= q128_s[e + 1]) ++e;
-                ex = e;
-                st = offs_s[e] + static_cast<std::uint32_t>(i - q128_s[e]) * 128u;
-            }
-            if (a.we128) a.we128[i] = ex;
-            if (a.ws128) a.ws128[i] = st;
-        }
-    }
+    fill_queues(a, sc, static_cast<std::size_t>(blockIdx.x) * kTile + threadIdx.x,
+                static_cast<std::size_t>(gridDim.x) * kTile);
 }
 
 // ---- gated SiLU -------------------------------------------------------------

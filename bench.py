@@ -220,10 +220,13 @@ def run_ours(args):
         if dist:
             dist.barrier()
     ms = ev[0].elapsed_time(ev[args.steps])
+    rank_ms = [ms]
     if dist:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        t = torch.zeros(world, device=dev, dtype=torch.float64)
+        t[rank] = ms
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        rank_ms = t.tolist()
+        ms = max(rank_ms)
     ms_per_step = ms / args.steps
 
     # per-kernel durations: the dominant kernel from the timed region; every
@@ -309,6 +312,7 @@ def run_ours(args):
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 3),
+            "ms_per_step_by_rank": [round(x / args.steps, 3) for x in rank_ms],
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,

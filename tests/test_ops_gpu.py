@@ -199,16 +199,18 @@ def _route_and_compare(ops, cuda, logits):
     return got
 
 
-@pytest.mark.parametrize("T", [1, 255, 256, 257, 8192, 100003])
+# Sizes around the 256-token tile boundaries and both sides of 16384.
+@pytest.mark.parametrize("T", [1, 31, 255, 256, 257, 1025, 4096, 8192, 12289, 16384, 16385, 100003])
 def test_moe_route_bitexact(ops, cuda, T):
     g = rng(5)
     _route_and_compare(ops, cuda, normal(g, (T, 16)))
 
 
+@pytest.mark.parametrize("T", [3000, 20000])
 @pytest.mark.parametrize("E", [2, 8, 13, 32])
-def test_moe_route_expert_counts(ops, cuda, E):
+def test_moe_route_expert_counts(ops, cuda, E, T):
     g = rng(6)
-    _route_and_compare(ops, cuda, normal(g, (3000, E)))
+    _route_and_compare(ops, cuda, normal(g, (T, E)))
 
 
 def test_moe_route_ties_and_quantum(ops, cuda):
