@@ -254,15 +254,67 @@ def slice_standins(s: StandIns, r0: int, rows: int) -> StandIns:
                     s.gate_up[2 * r0:2 * (r0 + rows)], s.expert_out[2 * r0:2 * (r0 + rows)])
 
 
+class HostStage:
+    """Uploads a chunk's trie index arrays for an end-to-end step: one
+    pinned host buffer per chunk (two, used alternately, so filling one never
+    waits for the copy out of the other), reused across steps, and one
+    asynchronous copy per chunk into a device buffer on the current stream."""
+
+    def __init__(self, device, batches: Sequence["Batch"]):
+        """Sizes the pinned buffers for `batches` (allocating pinned memory
+        inside a timed loop would stall it)."""
+        self.device = device
+        n = [2 * b.rows + b.tokens + len(b.prompts) for b in batches]
+        self.host = [[torch.empty(k, dtype=torch.int32, pin_memory=True) for k in n] for _ in range(2)]
+        self.done = [[None] * len(batches) for _ in range(2)]
+        self.slot = 0
+
+    def upload(self, c: int, prompts: Sequence[np.ndarray]) -> "Batch":
+        if c == 0:
+            self.slot ^= 1
+        trie = ops.prefix_trie(prompts)
+        lens = np.array([len(p) for p in prompts])
+        last = trie.token_node[np.cumsum(lens) - 1]
+        parts = [trie.node_token, trie.node_depth, trie.token_node, last]
+        n = sum(int(a.size) for a in parts)
+        if self.done[self.slot][c] is not None:
+            self.done[self.slot][c].synchronize()  # the copy that last read this buffer
+        buf = self.host[self.slot][c]
+        if buf is None or buf.numel() < n:
+            buf = self.host[self.slot][c] = torch.empty(n, dtype=torch.int32, pin_memory=True)
+        view = buf.numpy()
+        k = 0
+        for a in parts:
+            view[k:k + a.size] = a.view(np.int32)
+            k += a.size
+        dev = torch.empty(n, dtype=torch.int32, device=self.device)
+        dev.copy_(buf[:n], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self.done[self.slot][c] = ev
+        out, k = [], 0
+        for a in parts:
+            out.append(dev[k:k + a.size])
+            k += a.size
+        return Batch(list(prompts), trie, out[0], out[1], out[2], out[3], int(lens.max()))
+
+
 class ShardedPrefill:
     """One rank's share of a prompt batch on one GPU, split into `chunks`
     sub-batches. Each chunk runs all layers (b2_prefill_layers), writes its
     final hidden states as token rows, and -- with world > 1 -- is gathered
     to rank 0 by NCCL on the collective's own stream while the next chunk
-    computes, so only the last chunk's gather is exposed."""
+    computes, so only the last chunk's gather is exposed.
+
+    With `concurrent` (default) the chunks run on their own streams, chunk 0
+    at the highest priority: its launches take the SMs first, and the later
+    chunks' CTAs fill the gaps it leaves (each launch's ramp and drain, which
+    at a few thousand rows per launch cost as much as a tenth of the step).
+    Chunk 0 still finishes first, so its gather still overlaps the rest."""
 
     def __init__(self, prompts: Sequence[np.ndarray], plan: list, weights: Weights, device,
-                 standins: Sequence[StandIns], layers: int, rank: int = 0, exact: bool = False, group=None):
+                 standins: Sequence[StandIns], layers: int, rank: int = 0, exact: bool = False, group=None,
+                 concurrent: bool = True):
         """`plan` is shard.chunk_plan(prompts, world, chunks): this rank runs
         plan[rank]; every rank's chunk c must have the same token count (the
         per-chunk gather moves equal-sized buffers)."""
@@ -288,6 +340,12 @@ class ShardedPrefill:
         self.recv = None
         if world > 1 and rank == 0:
             self.recv = [[torch.empty_like(t) for _ in range(world)] for t in self.send]
+        self._stage = HostStage(device, self.batches)
+        self._last_idx = None
+        self.streams = None
+        if concurrent and len(self.pipes) > 1:
+            _, high = torch.cuda.Stream.priority_range()  # (lowest, highest): lower value = higher priority
+            self.streams = [torch.cuda.Stream(device, priority=min(high + c, 0)) for c in range(len(self.pipes))]
 
     @staticmethod
     def rows_needed(prompts: Sequence[np.ndarray], parts: list) -> int:
@@ -297,30 +355,40 @@ class ShardedPrefill:
         return sum(launches_per_run(self.layers) + (0 if d else 1) for d in self.direct)
 
     def step(self, timers=None) -> None:
-        """Enqueues the whole share on the current stream (+ the gathers);
-        on return the current stream is ordered after every gather."""
+        """Enqueues the whole share (+ the gathers) after the work already on
+        the current stream; on return the current stream is ordered after
+        every chunk and every gather."""
         import torch.distributed as dist
 
+        cur = torch.cuda.current_stream(self.device)
         works = []
         for c, pipe in enumerate(self.pipes):
-            if self.direct[c]:
-                pipe.run(timer=timers[c] if timers else None, final_out=self.send[c])
-            else:
-                pipe.run(timer=timers[c] if timers else None)
-                pipe.expand_to_tokens(self.send[c])
-            if self.world > 1:
-                works.append(dist.gather(self.send[c], self.recv[c] if self.rank == 0 else None, dst=0,
-                                         group=self.group, async_op=True))
-        for w in works:
+            s = self.streams[c] if self.streams else cur
+            if s is not cur:
+                s.wait_stream(cur)
+            with torch.cuda.stream(s):
+                if self.direct[c]:
+                    pipe.run(stream=s, timer=timers[c] if timers else None, final_out=self.send[c])
+                else:
+                    pipe.run(stream=s, timer=timers[c] if timers else None)
+                    pipe.expand_to_tokens(self.send[c])
+                if self.world > 1:  # the collective's stream waits for s
+                    works.append(dist.gather(self.send[c], self.recv[c] if self.rank == 0 else None, dst=0,
+                                             group=self.group, async_op=True))
+        if self.streams:
+            for s in self.streams:
+                cur.wait_stream(s)
+        for w in works:  # cur waits for the collective's stream
             w.wait()
 
-    def rebuild(self, pinned: bool = True) -> int:
+    def rebuild(self) -> int:
         """The host part of an end-to-end step: rebuilds every chunk's trie
-        from host token ids and uploads its index arrays; returns the H2D
-        bytes."""
+        from host token ids and uploads its index arrays (one copy per chunk
+        from a reused pinned buffer, asynchronous on the current stream);
+        returns the H2D bytes."""
         nbytes = 0
         for c, ps in enumerate(self.prompts):
-            b = Batch.build(ps, self.device, pinned=pinned)
+            b = self._stage.upload(c, ps)
             self.pipes[c].batch = b
             self.batches[c] = b
             nbytes += sum(int(t.numel()) * 4 for t in (b.node_token, b.node_depth, b.token_node, b.last_rows))
@@ -328,15 +396,19 @@ class ShardedPrefill:
 
     def last_token_rows(self, out: torch.Tensor) -> None:
         """Rank 0, after step(): the final hidden state of every prompt's last
-        token, for all ranks' prompts, in shard.gather_order(plan) order."""
+        token, for all ranks' prompts, in shard.gather_order(plan) order
+        (asynchronous: the row indices were uploaded once)."""
+        if self._last_idx is None:
+            self._last_idx = []
+            for c in range(len(self.batches)):
+                for r in range(self.world):
+                    ends = np.cumsum([len(self.all_prompts[i]) for i in self.plan[r][c]]) - 1
+                    self._last_idx.append((c, r, torch.from_numpy(ends.astype(np.int32)).to(self.device)))
         k = 0
-        for c in range(len(self.batches)):
-            for r in range(self.world):
-                ends = np.cumsum([len(self.all_prompts[i]) for i in self.plan[r][c]]) - 1
-                idx = torch.from_numpy(ends.astype(np.int32)).to(self.device)
-                src = self.recv[c][r] if self.recv is not None else self.send[c]
-                ops.gather_rows_gpu(src, idx, out[k:k + ends.size])
-                k += ends.size
+        for c, r, idx in self._last_idx:
+            src = self.recv[c][r] if self.recv is not None else self.send[c]
+            ops.gather_rows_gpu(src, idx, out[k:k + idx.numel()])
+            k += idx.numel()
 
 
 class StageTimer:

@@ -45,7 +45,9 @@ def split_by_fraction(prompts: Sequence[Sequence[int]], idx: Sequence[int],
     c, filled = 0, 0.0
     for g in groups.values():
         size = sum(len(prompts[i]) for i in g)
-        while c < len(parts) - 1 and filled >= targets[c] - 1e-9:
+        # next part once this group would overshoot the target by more than
+        # half of its own size
+        while c < len(parts) - 1 and filled + size / 2 > targets[c]:
             c, filled = c + 1, 0.0
         parts[c].extend(g)
         filled += size

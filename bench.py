@@ -53,9 +53,12 @@ def parse():
     p.add_argument("--length", type=int, default=2048)
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--pool", type=int, default=0, help="stand-in sets (0 = fit to memory)")
-    p.add_argument("--chunks", type=int, default=0, help="sub-batches per rank (0 = 1 on one GPU, 2 otherwise)")
-    p.add_argument("--first-chunk", type=float, default=0.75,
-                   help="share of a rank's tokens in its first sub-batch when there are 2")
+    p.add_argument("--chunks", type=int, default=0, help="sub-batches per rank (0 = 1 on one GPU, 3 otherwise)")
+    p.add_argument("--serial-chunks", action="store_true",
+                   help="run a rank's chunks one after another on one stream (default: concurrent streams, "
+                        "chunk 0 at the highest priority)")
+    p.add_argument("--chunk-fractions", default="",
+                   help="comma-separated shares of a rank's tokens per sub-batch, in order (default: balanced)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-kernel-timing", action="store_true",
                    help="no per-launch events in the timed region (diagnostic; the line then lacks kernels/roofline)")
@@ -175,8 +178,8 @@ def run_ours(args):
 
     prompts = prefill.prompts_config5(batch=args.prompts, length=args.length)
     tokens_total = sum(len(p) for p in prompts)
-    chunks = args.chunks or (1 if world == 1 else 2)
-    fractions = (args.first_chunk, 1.0 - args.first_chunk) if chunks == 2 else None
+    chunks = args.chunks or (1 if world == 1 else 3)
+    fractions = [float(f) for f in args.chunk_fractions.split(",")] if args.chunk_fractions else None
     plan = chunk_plan(prompts, world, chunks, fractions)
     sizes = {tuple(sum(len(prompts[i]) for i in part) for part in parts) for parts in plan}
     if len(sizes) != 1:
@@ -193,7 +196,8 @@ def run_ours(args):
     standins = [StandIns.make(rows, dev, gen) for _ in range(pool)]
     torch.cuda.synchronize()
     t_gen = time.perf_counter() - t_gen
-    runner = ShardedPrefill(prompts, plan, weights, dev, standins, args.layers, rank=rank, exact=args.exact)
+    runner = ShardedPrefill(prompts, plan, weights, dev, standins, args.layers, rank=rank, exact=args.exact,
+                            concurrent=not args.serial_chunks)
     stream = torch.cuda.current_stream(dev)
 
     for _ in range(args.warmup):
@@ -261,18 +265,19 @@ def run_ours(args):
     host_last = torch.empty((args.prompts, prefill.HIDDEN), pin_memory=True)
 
     def e2e_step():
-        h2d = runner.rebuild(pinned=True)
+        h2d = runner.rebuild()
         runner.step()
         if rank == 0:
             runner.last_token_rows(last)
             host_last.copy_(last, non_blocking=True)
         return h2d
 
-    e2e_step()
+    for _ in range(2):  # both pinned staging buffers in use once
+        e2e_step()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    e2e_steps = max(1, min(args.steps, 3))
+    e2e_steps = args.steps
     e2e_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     e2e_ev[0].record(stream)
     for _ in range(e2e_steps):
@@ -332,7 +337,9 @@ def run_ours(args):
                          "peak_kind": peak_kind, "traffic": traffic},
             "kernels": kern,
             "kernels_note": "per launch kind: one fully instrumented step after the timed region; the dominant "
-                            "kind (roofline) from events in the timed region",
+                            "kind (roofline) from events in the timed region" +
+                            ("; chunks run concurrently, so a launch's events also span the other chunks' "
+                             "kernels sharing the GPU" if runner.streams else ""),
             "clocks": {"sm_mhz": statistics.median(mhz) if mhz else None,
                        "sm_max_mhz": allclk[0].get("sm_max_mhz"), "reasons": reasons},
             "e2e": {"value": round(tokens_total / (e2e_ms / 1e3), 1), "unit": "tokens/s",

@@ -122,3 +122,23 @@ def test_two_cpu_ranks_gather_matches_single_process(tmp_path):
     order = gather_order(plan)
     want = np.concatenate([_run_chunk(prompts, [i]) for i in order])
     np.testing.assert_array_equal(got, want)
+
+
+def test_chunk_plan_fractions():
+    from aps2026_b200.shard import chunk_plan
+
+    prompts = [np.full(2048, i, dtype=np.int32) for i in range(64)]
+    for fr, want in (((0.75, 0.25), [6, 2]), ((0.5, 0.5), [4, 4]), ((0.4, 0.35, 0.25), [3, 3, 2]),
+                     ((0.5, 0.3, 0.2), [4, 2, 2])):
+        plan = chunk_plan(prompts, 8, len(fr), fr)
+        for parts in plan:
+            assert [len(p) for p in parts] == want
+            flat = [i for p in parts for i in p]
+            assert flat == sorted(flat)  # consecutive, in order
+        assert sorted(i for parts in plan for p in parts for i in p) == list(range(64))
+    # prompts sharing a first token stay in one chunk
+    same = [np.array([7, 1, 2]), np.array([7, 1, 3]), np.array([9, 9]), np.array([5, 5])]
+    plan = chunk_plan(same, 1, 2, (0.5, 0.5))
+    assert any({0, 1} <= set(p) for p in plan[0])
+    with pytest.raises(ValueError):
+        chunk_plan(prompts, 2, 3, (0.5, 0.5))

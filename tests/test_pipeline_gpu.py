@@ -90,3 +90,66 @@ def test_expand_and_last_rows(cuda):
     oracle.assert_bitexact(to_host(tokens), want_y[tn], "expanded rows")
     ends = np.cumsum([len(p) for p in prompts]) - 1
     oracle.assert_bitexact(to_host(last), want_y[tn[ends]], "last-token rows")
+
+
+def _grouped_prompts(seed=13):
+    """Six prompts in three first-token groups (3 + 2 + 1) with shared
+    prefixes inside each group, so chunks hold whole groups and node rows
+    differ from token rows."""
+    from aps2026_b200 import prefill
+
+    g = np.random.default_rng(seed)
+    out = []
+    for n, shared in ((3, 10), (2, 20), (1, 0)):
+        prefix = g.integers(0, prefill.VOCAB, max(shared, 1))
+        for _ in range(n):
+            out.append(np.concatenate([prefix, g.integers(0, prefill.VOCAB, 48 - prefix.size)]).astype(np.int32))
+    return out
+
+
+def _sharded(cuda, prompts, plan, concurrent, layers=2, pool=2):
+    import torch
+
+    from aps2026_b200 import prefill
+
+    w = prefill.Weights.make(cuda, 9, layers=layers)
+    rows = prefill.ShardedPrefill.rows_needed(prompts, plan[0])
+    gen = torch.Generator(device=cuda).manual_seed(21)  # same stand-ins for every runner
+    sets = [prefill.StandIns.make(rows, cuda, gen) for _ in range(pool)]
+    return prefill.ShardedPrefill(prompts, plan, w, cuda, sets, layers, exact=True, concurrent=concurrent)
+
+
+def test_sharded_concurrent_chunks_match_serial_and_rebuild(cuda):
+    """One rank, three chunks: chunks on concurrent prioritised streams give
+    the same token rows as one stream, bit for bit; so does an end-to-end
+    step whose tries are rebuilt on the host and uploaded from the reused
+    pinned buffers (rebuilt twice, to cycle both buffers)."""
+    import torch
+
+    from aps2026_b200.shard import chunk_plan
+
+    prompts = _grouped_prompts()
+    plan = chunk_plan(prompts, 1, 3)
+    assert len(plan[0]) == 3
+    serial = _sharded(cuda, prompts, plan, concurrent=False)
+    serial.step()
+    conc = _sharded(cuda, prompts, plan, concurrent=True)
+    assert conc.streams is not None
+    conc.step()
+    e2e = _sharded(cuda, prompts, plan, concurrent=True)
+    for _ in range(2):
+        e2e.rebuild()
+        for b, b0 in zip(e2e.batches, serial.batches):
+            for name in ("node_token", "node_depth", "token_node", "last_rows"):
+                assert torch.equal(getattr(b, name), getattr(b0, name)), name
+    e2e.step()
+    torch.cuda.synchronize()
+    for c in range(3):
+        assert torch.equal(conc.send[c], serial.send[c]), f"chunk {c}: concurrent != serial"
+        assert torch.equal(e2e.send[c], serial.send[c]), f"chunk {c}: rebuilt != built"
+    last = torch.empty((len(prompts), 4096), device=cuda)
+    want = torch.empty_like(last)
+    e2e.last_token_rows(last)
+    serial.last_token_rows(want)
+    torch.cuda.synchronize()
+    assert torch.equal(last, want)
