@@ -218,6 +218,311 @@ attention_tree_kernel(AttnArgs a) {
         for (int g = 0; g < kGroup; ++g) out_row[g * HD + d] = value[g];
 }
 
+// ---- query-blocked kernel (head_dim 128) --------------------------------------
+//
+// The rows of a trie path -- node n + 1 the child of node n, as prefix-trie
+// numbering makes every run of new nodes along one prompt -- have nested
+// ancestor chains: the chain of the deepest row holds every other row's
+// keys. attention_tree_block gives one CTA a block of kBlkRows such rows and
+// one KV head, stages each K and V tile of that chain once for all of them,
+// and keeps each lane's query slices in registers, so every value read from
+// shared memory feeds 8 (QK) or 4 (PV) fused multiply-adds. The arithmetic
+// per (row, head) is the reference's, in its order: four accumulators over
+// d mod 4 (chain j sums q[d] k[d] for d = j, j + 4, ... in ascending d, one
+// lane per chain), combined ((a0 + a1) + (a2 + a3)) by shuffles, times the
+// scale; the softmax over the row's own window; the output a fused
+// multiply-add chain over the window in ascending key order.
+// Blocks that are not a path (prompt starts, bad positions, or an ancestor
+// table whose rows disagree) fall back to one row at a time in the same code.
+constexpr int kBlkRows = 4;                    // query rows per CTA
+constexpr int kBlkThreads = 256;
+constexpr int kBlkKeys = 64;                   // chain keys per staged tile
+constexpr int kCombos = kBlkRows * kGroup;     // (row, head) pairs: 16
+constexpr int kJStride = 36;                   // floats between the 4 d-mod-4 slices of a staged key
+constexpr int kKeyPitch = 4 * kJStride;        // floats per staged key (also holds a value row)
+
+// Shared layout (floats): scores [wcap][16] | chain [wcap] (u32) | tile [64][144].
+inline std::size_t block_smem_bytes(std::size_t wcap) {
+    return (wcap * kCombos + wcap + static_cast<std::size_t>(kBlkKeys) * kKeyPitch) * 4;
+}
+
+template <bool EXACT>
+struct BlockAttention {
+    const AttnArgs& a;
+    float* scores;
+    std::uint32_t* chain;
+    float* tile;
+    const double* tab;
+    float* red;  // [8 warps][16 combos] reduction scratch
+    std::size_t kh;
+    unsigned tid, lane, warp;
+
+    // Stages the 64 chain rows of tile t (K transposed to [key][j][i],
+    // d = 4i + j, or V as [key][d]) from registers filled by fetch().
+    __device__ __forceinline__ void fetch(const float* base, int t, int wg, float4 (&pre)[8]) const {
+        const std::size_t row4 = a.kv_heads * 128 / 4;
+        const float4* src = reinterpret_cast<const float4*>(base + kh * 128);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = static_cast<int>(tid) + u * kBlkThreads, ks = i >> 5, c = i & 31;
+            const int w = t * kBlkKeys + ks;
+            pre[u] = w < wg ? __ldg(src + static_cast<std::size_t>(chain[w]) * row4 + c)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    __device__ __forceinline__ void store_keys(const float4 (&pre)[8]) const {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = static_cast<int>(tid) + u * kBlkThreads, ks = i >> 5, c = i & 31;
+            float* dst = tile + ks * kKeyPitch + c;
+            dst[0] = pre[u].x;
+            dst[kJStride] = pre[u].y;
+            dst[2 * kJStride] = pre[u].z;
+            dst[3 * kJStride] = pre[u].w;
+        }
+    }
+    __device__ __forceinline__ void store_values(const float4 (&pre)[8]) const {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = static_cast<int>(tid) + u * kBlkThreads, ks = i >> 5, c = i & 31;
+            reinterpret_cast<float4*>(tile + ks * kKeyPitch)[c] = pre[u];
+        }
+    }
+
+    // Rows first .. first + g - 1 (a path, g <= kBlkRows). With `verify`,
+    // returns false (computing nothing) when some row's ancestors in its
+    // window differ from the deepest row's.
+    __device__ bool run(std::size_t first, int g, bool verify) const {
+        const std::size_t last = first + g - 1;
+        const std::size_t p0 = a.row_pos[first], P = a.row_pos[last];
+        const std::size_t begin = p0 + 1 > a.window ? p0 + 1 - a.window : 0;
+        const int wg = static_cast<int>(P - begin + 1);
+        const std::uint32_t* anc_last = a.anc + last * a.anc_stride + begin;
+        for (int i = tid; i < wg; i += kBlkThreads) {
+            std::uint32_t c = anc_last[i];
+            if (c >= a.rows) {
+                flag_check(B2_CHECK_ATTENTION);
+                c = static_cast<std::uint32_t>(last);
+            }
+            chain[i] = c;
+        }
+        __syncthreads();  // chain complete (fetch reads other threads' entries)
+        if (verify && g > 1) {
+            int differs = 0;
+            for (int r = 0; r + 1 < g; ++r) {
+                const std::size_t pr = p0 + r;
+                const std::size_t br = pr + 1 > a.window ? pr + 1 - a.window : 0;
+                const std::uint32_t* own = a.anc + (first + r) * a.anc_stride;
+                for (std::size_t k = br + tid; k <= pr; k += kBlkThreads)
+                    differs |= own[k] != anc_last[k - begin];
+            }
+            if (__syncthreads_or(differs)) return false;
+        }
+
+        // ---- scores[w][r * 4 + h] ----
+        const unsigned j = lane & 3, cp = lane >> 2;        // chain j; combos 2cp, 2cp + 1
+        const int rq = static_cast<int>(cp >> 1), hq = static_cast<int>(cp & 1) * 2;
+        float qa[32], qb[32];
+        {
+            const std::size_t qrow = first + (rq < g ? rq : g - 1);
+            const float* q0 = a.q + (qrow * a.q_heads + kh * kGroup + hq) * 128 + j;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                qa[i] = __ldg(q0 + 4 * i);
+                qb[i] = __ldg(q0 + 128 + 4 * i);
+            }
+        }
+        const int tiles = (wg + kBlkKeys - 1) / kBlkKeys;
+        float4 pre[8];
+        fetch(a.k, 0, wg, pre);
+        for (int t = 0; t < tiles; ++t) {
+            __syncthreads();  // the previous tile has been read
+            store_keys(pre);
+            __syncthreads();
+            if (t + 1 < tiles) fetch(a.k, t + 1, wg, pre);
+#pragma unroll 1
+            for (int m = 0; m < kBlkKeys / 16; ++m) {
+                const int ka = static_cast<int>(warp) + 16 * m, kb = ka + 8;  // this warp's two keys
+                const int wa = t * kBlkKeys + ka;
+                if (wa >= wg) break;
+                const float4* xa = reinterpret_cast<const float4*>(tile + ka * kKeyPitch + j * kJStride);
+                const float4* xb = reinterpret_cast<const float4*>(tile + kb * kKeyPitch + j * kJStride);
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;   // (a, combo 0), (a, 1), (b, 0), (b, 1)
+#pragma unroll
+                for (int t4 = 0; t4 < 8; ++t4) {
+                    const float4 x = xa[t4], y = xb[t4];
+                    s0 = __fmaf_rn(qa[4 * t4], x.x, s0); s0 = __fmaf_rn(qa[4 * t4 + 1], x.y, s0);
+                    s0 = __fmaf_rn(qa[4 * t4 + 2], x.z, s0); s0 = __fmaf_rn(qa[4 * t4 + 3], x.w, s0);
+                    s1 = __fmaf_rn(qb[4 * t4], x.x, s1); s1 = __fmaf_rn(qb[4 * t4 + 1], x.y, s1);
+                    s1 = __fmaf_rn(qb[4 * t4 + 2], x.z, s1); s1 = __fmaf_rn(qb[4 * t4 + 3], x.w, s1);
+                    s2 = __fmaf_rn(qa[4 * t4], y.x, s2); s2 = __fmaf_rn(qa[4 * t4 + 1], y.y, s2);
+                    s2 = __fmaf_rn(qa[4 * t4 + 2], y.z, s2); s2 = __fmaf_rn(qa[4 * t4 + 3], y.w, s2);
+                    s3 = __fmaf_rn(qb[4 * t4], y.x, s3); s3 = __fmaf_rn(qb[4 * t4 + 1], y.y, s3);
+                    s3 = __fmaf_rn(qb[4 * t4 + 2], y.z, s3); s3 = __fmaf_rn(qb[4 * t4 + 3], y.w, s3);
+                }
+                // ((a0 + a1) + (a2 + a3)) across the four chain lanes
+                s0 = __fadd_rn(s0, __shfl_xor_sync(0xffffffffu, s0, 1));
+                s1 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 1));
+                s2 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 1));
+                s3 = __fadd_rn(s3, __shfl_xor_sync(0xffffffffu, s3, 1));
+                s0 = __fadd_rn(s0, __shfl_xor_sync(0xffffffffu, s0, 2));
+                s1 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 2));
+                s2 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 2));
+                s3 = __fadd_rn(s3, __shfl_xor_sync(0xffffffffu, s3, 2));
+                if (j == 0) {
+                    float* sa = scores + static_cast<std::size_t>(wa) * kCombos + 2 * cp;
+                    sa[0] = __fmul_rn(s0, a.scale);
+                    sa[1] = __fmul_rn(s1, a.scale);
+                    if (wa + 8 < wg) {
+                        sa[8 * kCombos] = __fmul_rn(s2, a.scale);
+                        sa[8 * kCombos + 1] = __fmul_rn(s3, a.scale);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+
+        // ---- softmax of every (row, head) over the row's window: warp `warp`
+        // takes keys [wg * warp / 8, wg * (warp + 1) / 8), lane (combo c,
+        // parity) every other key of them, so each access is two whole
+        // 64-byte score rows (no bank conflicts) ----
+        {
+            const int c = static_cast<int>(lane & 15), par = static_cast<int>(lane >> 4), rc = c >> 2;
+            int lo = 1, hi = 0;  // empty for rows past the group
+            if (rc < g) {
+                const std::size_t pr = p0 + rc;
+                lo = static_cast<int>((pr + 1 > a.window ? pr + 1 - a.window : 0) - begin);
+                hi = static_cast<int>(pr - begin);
+            }
+            const int wb = max(wg * static_cast<int>(warp) / 8, lo);
+            const int we = min(wg * (static_cast<int>(warp) + 1) / 8 - 1, hi);
+            float m = -3.402823466e+38F;
+            for (int w = wb + par; w <= we; w += 2) m = fmaxf(m, scores[w * kCombos + c]);
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+            if (lane < 16) red[warp * 16 + c] = m;
+            __syncthreads();
+            m = red[c];
+#pragma unroll
+            for (int k = 1; k < 8; ++k) m = fmaxf(m, red[k * 16 + c]);
+            __syncthreads();  // red is reused
+            float part = 0.0f;
+            for (int w = wb + par; w <= we; w += 2) {
+                const float e = exp_ref(__fsub_rn(scores[w * kCombos + c], m), tab);
+                scores[w * kCombos + c] = e;
+                part = __fadd_rn(part, e);
+            }
+            float d;
+            if (EXACT) {  // serial ascending sums, one lane per (row, head)
+                __syncthreads();
+                if (warp == 0 && lane < 16) {
+                    float acc = 0.0f;
+#pragma unroll 8
+                    for (int w = lo; w <= hi; ++w) acc = __fadd_rn(acc, scores[w * kCombos + c]);
+                    red[c] = acc;
+                }
+                __syncthreads();
+                d = red[c];
+            } else {
+                part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, 16));
+                if (lane < 16) red[warp * 16 + c] = part;
+                __syncthreads();
+                d = red[c];
+#pragma unroll
+                for (int k = 1; k < 8; ++k) d = __fadd_rn(d, red[k * 16 + c]);
+            }
+            const float y = __frcp_rn(d);
+            for (int w = wb + par; w <= we; w += 2)
+                scores[w * kCombos + c] = attn_div(scores[w * kCombos + c], d, y);
+        }
+
+        // ---- out[r][h][d] = sum_w p[w][r * 4 + h] v[w][d], ascending w ----
+        const int rp = static_cast<int>(tid >> 6), dp = static_cast<int>(tid & 63);  // row; d pair
+        const std::size_t prp = p0 + rp;
+        const int plo = static_cast<int>((prp + 1 > a.window ? prp + 1 - a.window : 0) - begin);
+        const int phi = static_cast<int>(prp - begin);
+        float acc[kGroup][2] = {};
+        fetch(a.v, 0, wg, pre);
+        for (int t = 0; t < tiles; ++t) {
+            __syncthreads();  // softmax done / the previous tile has been read
+            store_values(pre);
+            __syncthreads();
+            if (t + 1 < tiles) fetch(a.v, t + 1, wg, pre);
+            if (rp < g) {
+                const int w0 = max(plo - t * kBlkKeys, 0), w1 = min(phi - t * kBlkKeys, kBlkKeys - 1);
+                const float* prow = scores + static_cast<std::size_t>(t * kBlkKeys) * kCombos + 4 * rp;
+#pragma unroll 4
+                for (int w = w0; w <= w1; ++w) {
+                    const float4 pw = *reinterpret_cast<const float4*>(prow + w * kCombos);
+                    const float2 vv = *reinterpret_cast<const float2*>(tile + w * kKeyPitch + 2 * dp);
+                    acc[0][0] = __fmaf_rn(pw.x, vv.x, acc[0][0]);
+                    acc[0][1] = __fmaf_rn(pw.x, vv.y, acc[0][1]);
+                    acc[1][0] = __fmaf_rn(pw.y, vv.x, acc[1][0]);
+                    acc[1][1] = __fmaf_rn(pw.y, vv.y, acc[1][1]);
+                    acc[2][0] = __fmaf_rn(pw.z, vv.x, acc[2][0]);
+                    acc[2][1] = __fmaf_rn(pw.z, vv.y, acc[2][1]);
+                    acc[3][0] = __fmaf_rn(pw.w, vv.x, acc[3][0]);
+                    acc[3][1] = __fmaf_rn(pw.w, vv.y, acc[3][1]);
+                }
+            }
+        }
+        if (rp < g) {
+            float* o = a.out + ((first + rp) * a.q_heads + kh * kGroup) * 128 + 2 * dp;
+#pragma unroll
+            for (int h = 0; h < kGroup; ++h)
+                *reinterpret_cast<float2*>(o + h * 128) = make_float2(acc[h][0], acc[h][1]);
+        }
+        __syncthreads();  // scores / chain / tile are reused by the next group
+        return true;
+    }
+};
+
+template <bool EXACT>
+__global__ void __launch_bounds__(kBlkThreads, 1)
+attention_tree_block(AttnArgs a, std::size_t wcap) {
+    pdl_begin();
+    extern __shared__ __align__(16) float smem[];
+    __shared__ double tab[64];
+    __shared__ int seg_s[kBlkRows + 1], bad_s[kBlkRows], nseg_s;
+    __shared__ float red_s[(kBlkThreads / 32) * kCombos];
+    load_exp2_table(tab);
+    const std::size_t kh = blockIdx.x % a.kv_heads;
+    const std::size_t n0 = (blockIdx.x / a.kv_heads) * kBlkRows;
+    const int nrows = static_cast<int>(a.rows - n0 < kBlkRows ? a.rows - n0 : kBlkRows);
+    if (threadIdx.x == 0) {
+        // segments: maximal runs in which row n is the child of row n - 1
+        int nseg = 0;
+        seg_s[0] = 0;
+        std::size_t prev = 0;
+        for (int r = 0; r < nrows; ++r) {
+            const std::size_t pos = a.row_pos[n0 + r];
+            bad_s[r] = pos >= a.anc_stride;
+            if (r > 0) {
+                const bool link = !bad_s[r] && !bad_s[r - 1] && pos == prev + 1 &&
+                                  a.anc[(n0 + r) * a.anc_stride + pos - 1] == n0 + r - 1;
+                if (!link) seg_s[++nseg] = r;
+            }
+            prev = pos;
+        }
+        seg_s[++nseg] = nrows;
+        nseg_s = nseg;
+    }
+    __syncthreads();
+    BlockAttention<EXACT> b{a, smem, reinterpret_cast<std::uint32_t*>(smem + wcap * kCombos),
+                            smem + wcap * kCombos + wcap, tab, red_s, kh,
+                            threadIdx.x, threadIdx.x & 31u, threadIdx.x >> 5};
+    for (int sgi = 0; sgi < nseg_s; ++sgi) {
+        const int r0 = seg_s[sgi], r1 = seg_s[sgi + 1];
+        if (r1 - r0 == 1 && bad_s[r0]) {  // position outside the ancestor table: report, output zeros
+            if (threadIdx.x == 0) flag_check(B2_CHECK_ATTENTION);
+            float* o = a.out + ((n0 + r0) * a.q_heads + kh * kGroup) * 128;
+            for (int i = threadIdx.x; i < kGroup * 128; i += kBlkThreads) o[i] = 0.0f;
+            continue;
+        }
+        if (!b.run(n0 + r0, r1 - r0, true))
+            for (int r = r0; r < r1; ++r) b.run(n0 + r, 1, false);
+    }
+}
+
 template <int HD, bool EXACT>
 int launch_attention(const AttnArgs& a, cudaStream_t s) {
     const std::size_t chain_words = (a.max_window + 3) & ~std::size_t(3);
@@ -253,6 +558,17 @@ extern "C" int b2_attention_tree(const float* q, const float* k, const float* v,
                window < anc_stride ? window : anc_stride, 1.0f / sqrtf(static_cast<float>(head_dim))};
     const bool exact = (flags & B2_FLAG_EXACT_ORDER) != 0;
     cudaStream_t s = as_stream(stream);
+    const std::size_t wcap = (a.max_window + kBlkRows - 1 + 3) & ~std::size_t(3);
+    if (head_dim == 128 && block_smem_bytes(wcap) <= 200 * 1024 && aligned16(q) && aligned16(out) &&
+        (rows + kBlkRows - 1) / kBlkRows * kv_heads <= 0x7FFFFFFFu) {
+        const std::size_t smem = block_smem_bytes(wcap);
+        auto kernel = exact ? attention_tree_block<true> : attention_tree_block<false>;
+        if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
+            return launch_result("b2_attention_tree: shared memory attribute");
+        launch_pdl(kernel, static_cast<unsigned>((rows + kBlkRows - 1) / kBlkRows * kv_heads), kBlkThreads, smem,
+                   s, a, wcap);
+        return launch_result("b2_attention_tree");
+    }
     int rc;
     if (head_dim == 128) rc = exact ? launch_attention<128, true>(a, s) : launch_attention<128, false>(a, s);
     else rc = exact ? launch_attention<64, true>(a, s) : launch_attention<64, false>(a, s);

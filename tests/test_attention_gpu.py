@@ -24,19 +24,24 @@ def _case(seed, prompts, length, shared, q_heads=16, kv_heads=4, hd=128):
     return t, q, k, v
 
 
-@pytest.mark.parametrize("prompts,length,shared,window", [(3, 300, 40, 2047), (2, 700, 10, 100), (1, 5, 0, 2047)])
+# head_dim 128 runs the query-blocked kernel (4 path rows per CTA), 64 the
+# per-row kernel; lengths not divisible by 4 leave partial blocks and blocks
+# that straddle prompt starts; window 100 < depth.
+@pytest.mark.parametrize("prompts,length,shared,window,hd", [(3, 300, 40, 2047, 128), (2, 700, 10, 100, 128),
+                                                              (1, 5, 0, 2047, 128), (5, 37, 3, 2047, 128),
+                                                              (3, 130, 20, 50, 64)])
 @pytest.mark.parametrize("exact", [True, False])
-def test_attention_tree_vs_oracle(cuda, prompts, length, shared, window, exact):
+def test_attention_tree_vs_oracle(cuda, prompts, length, shared, window, hd, exact):
     import torch
 
     from aps2026_b200 import ops
 
-    t, q, k, v = _case(50, prompts, length, shared)
+    t, q, k, v = _case(50, prompts, length, shared, hd=hd)
     R, stride = t["nodes"], t["node_anc"].shape[1]
-    want = oracle.attention_tree(q, k, v, t["node_depth"], t["node_anc"], 16, 4, 128, window)
-    out = torch.full((R, 16 * 128), float("nan"), device=cuda)
+    want = oracle.attention_tree(q, k, v, t["node_depth"], t["node_anc"], 16, 4, hd, window)
+    out = torch.full((R, 16 * hd), float("nan"), device=cuda)
     pos, anc = to_dev(t["node_depth"], cuda), to_dev(np.ascontiguousarray(t["node_anc"]), cuda)
-    ops.attention_tree_gpu(to_dev(q, cuda), to_dev(k, cuda), to_dev(v, cuda), out, pos, anc, stride, R, 16, 4, 128,
+    ops.attention_tree_gpu(to_dev(q, cuda), to_dev(k, cuda), to_dev(v, cuda), out, pos, anc, stride, R, 16, 4, hd,
                            window, exact=exact)
     torch.cuda.synchronize()
     if exact:
@@ -87,3 +92,24 @@ def test_attention_tree_bad_index_is_reported(cuda):
     status = ops.device_status()
     assert status & 8
     assert torch.equal(out[7], torch.zeros_like(out[7]))
+
+
+def test_attention_tree_inconsistent_ancestors_fall_back_per_row(cuda):
+    """Rows linked as parent and child whose ancestor rows disagree further
+    up (not a trie's table) are computed one row at a time, each from its
+    own ancestor row, as the reference kernel reads them."""
+    import torch
+
+    from aps2026_b200 import ops
+
+    t, q, k, v = _case(53, 2, 60, 0)
+    R, stride = t["nodes"], t["node_anc"].shape[1]
+    anc = np.ascontiguousarray(t["node_anc"]).copy()
+    anc[10, 3] = 70  # a node of the other prompt, still a valid row
+    want = oracle.attention_tree(q, k, v, t["node_depth"], anc, 16, 4, 128, 2047)
+    out = torch.empty((R, 16 * 128), device=cuda)
+    ops.attention_tree_gpu(to_dev(q, cuda), to_dev(k, cuda), to_dev(v, cuda), out, to_dev(t["node_depth"], cuda),
+                           to_dev(anc, cuda), stride, R, 16, 4, 128, 2047, exact=True)
+    torch.cuda.synchronize()
+    oracle.assert_bitexact(to_host(out), want, "attention, inconsistent ancestors")
+    assert ops.device_status() == 0
