@@ -7,8 +7,11 @@
 // softmax on 4 threads, and reads V straight from global memory one scalar
 // per key per thread.
 //
-// Here, also one CTA per (row, KV head) with the same arithmetic in the
-// same order (so B2_FLAG_EXACT_ORDER output is bit-identical), but:
+// Two kernels with the reference's arithmetic in its order (so
+// B2_FLAG_EXACT_ORDER output is bit-identical). head_dim 128 runs the
+// query-blocked attention_tree_block below; other head dims (64) and
+// windows too large for its shared memory run attention_tree_kernel, one
+// CTA per (row, KV head) like the reference, but:
 //   - keys: tiles of 64 chain rows staged in shared memory with 128-bit
 //     loads (all of a thread's loads of a tile issued before any is
 //     stored), every thread computing one key for two of the four query
@@ -224,9 +227,11 @@ attention_tree_kernel(AttnArgs a) {
 // numbering makes every run of new nodes along one prompt -- have nested
 // ancestor chains: the chain of the deepest row holds every other row's
 // keys. attention_tree_block gives one CTA a block of kBlkRows such rows and
-// one KV head, stages each K and V tile of that chain once for all of them,
-// and keeps each lane's query slices in registers, so every value read from
-// shared memory feeds 8 (QK) or 4 (PV) fused multiply-adds. The arithmetic
+// one KV head, stages each K and V tile of that chain once for all of them
+// (cp.async into two alternating buffers, so no registers wait on the
+// copies and two CTAs fit an SM at a 1024-key window), and keeps each lane's
+// query slices in registers, so every value read from shared memory feeds 8
+// (QK) or 16 (PV) fused multiply-adds. The arithmetic
 // per (row, head) is the reference's, in its order: four accumulators over
 // d mod 4 (chain j sums q[d] k[d] for d = j, j + 4, ... in ascending d, one
 // lane per chain), combined ((a0 + a1) + (a2 + a3)) by shuffles, times the
@@ -236,15 +241,32 @@ attention_tree_kernel(AttnArgs a) {
 // table whose rows disagree) fall back to one row at a time in the same code.
 constexpr int kBlkRows = 4;                    // query rows per CTA
 constexpr int kBlkThreads = 256;
-constexpr int kBlkKeys = 64;                   // chain keys per staged tile
+constexpr int kBlkKeys = 32;                   // chain keys per staged tile (two tiles in flight)
 constexpr int kCombos = kBlkRows * kGroup;     // (row, head) pairs: 16
 constexpr int kJStride = 36;                   // floats between the 4 d-mod-4 slices of a staged key
 constexpr int kKeyPitch = 4 * kJStride;        // floats per staged key (also holds a value row)
+constexpr int kTileFloats = kBlkKeys * kKeyPitch;
 
-// Shared layout (floats): scores [wcap][16] | chain [wcap] (u32) | tile [64][144].
+// Shared layout (floats): scores [wcap][16] | chain [wcap] (u32) | 2 tiles [32][144].
+// At a 1024-key window that is 107 KB and two CTAs share an SM.
 inline std::size_t block_smem_bytes(std::size_t wcap) {
-    return (wcap * kCombos + wcap + static_cast<std::size_t>(kBlkKeys) * kKeyPitch) * 4;
+    return (wcap * kCombos + wcap + 2 * static_cast<std::size_t>(kTileFloats)) * 4;
 }
+
+// Asynchronous global -> shared copies (no registers held while in flight).
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(
+                     static_cast<unsigned>(__cvta_generic_to_shared(dst))), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(
+                     static_cast<unsigned>(__cvta_generic_to_shared(dst))), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
 template <bool EXACT>
 struct BlockAttention {
@@ -257,36 +279,41 @@ struct BlockAttention {
     std::size_t kh;
     unsigned tid, lane, warp;
 
-    // Stages the 64 chain rows of tile t (K transposed to [key][j][i],
-    // d = 4i + j, or V as [key][d]) from registers filled by fetch().
-    __device__ __forceinline__ void fetch(const float* base, int t, int wg, float4 (&pre)[8]) const {
-        const std::size_t row4 = a.kv_heads * 128 / 4;
-        const float4* src = reinterpret_cast<const float4*>(base + kh * 128);
+    // Issues the copies of the 32 chain rows of tile t into buffer t & 1:
+    // keys transposed to [key][j][i] (d = 4i + j), one 4-byte copy per
+    // element, consecutive threads on consecutive d of one key (coalesced;
+    // 16 consecutive d per thread measured 30% slower); values as [key][d],
+    // one 16-byte copy per 4 elements. Rows past wg are skipped.
+    __device__ __forceinline__ void issue_keys(int t, int wg) const {
+        const std::size_t row = a.kv_heads * 128;
+        float* buf = tile + (t & 1) * kTileFloats;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < kBlkKeys * 128 / kBlkThreads; ++u) {
+            const int i = static_cast<int>(tid) + u * kBlkThreads, ks = i >> 7, d = i & 127;
+            const int w = t * kBlkKeys + ks;
+            if (w < wg)
+                cp_async4(buf + ks * kKeyPitch + (d & 3) * kJStride + (d >> 2),
+                          a.k + static_cast<std::size_t>(chain[w]) * row + kh * 128 + d);
+        }
+        cp_async_commit();
+    }
+    __device__ __forceinline__ void issue_values(int t, int wg) const {
+        const std::size_t row = a.kv_heads * 128;
+        float* buf = tile + (t & 1) * kTileFloats;
+#pragma unroll
+        for (int u = 0; u < kBlkKeys * 32 / kBlkThreads; ++u) {
             const int i = static_cast<int>(tid) + u * kBlkThreads, ks = i >> 5, c = i & 31;
             const int w = t * kBlkKeys + ks;
-            pre[u] = w < wg ? __ldg(src + static_cast<std::size_t>(chain[w]) * row4 + c)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (w < wg)
+                cp_async16(buf + ks * kKeyPitch + 4 * c, a.v + static_cast<std::size_t>(chain[w]) * row + kh * 128 + 4 * c);
         }
+        cp_async_commit();
     }
-    __device__ __forceinline__ void store_keys(const float4 (&pre)[8]) const {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = static_cast<int>(tid) + u * kBlkThreads, ks = i >> 5, c = i & 31;
-            float* dst = tile + ks * kKeyPitch + c;
-            dst[0] = pre[u].x;
-            dst[kJStride] = pre[u].y;
-            dst[2 * kJStride] = pre[u].z;
-            dst[3 * kJStride] = pre[u].w;
-        }
-    }
-    __device__ __forceinline__ void store_values(const float4 (&pre)[8]) const {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = static_cast<int>(tid) + u * kBlkThreads, ks = i >> 5, c = i & 31;
-            reinterpret_cast<float4*>(tile + ks * kKeyPitch)[c] = pre[u];
-        }
+    // Tile t has landed for every thread (the next one may still be in flight).
+    __device__ __forceinline__ void tile_ready(int t, int tiles) const {
+        if (t + 1 < tiles) cp_async_wait<1>();
+        else cp_async_wait<0>();
+        __syncthreads();
     }
 
     // Rows first .. first + g - 1 (a path, g <= kBlkRows). With `verify`,
@@ -333,20 +360,18 @@ struct BlockAttention {
             }
         }
         const int tiles = (wg + kBlkKeys - 1) / kBlkKeys;
-        float4 pre[8];
-        fetch(a.k, 0, wg, pre);
+        issue_keys(0, wg);
         for (int t = 0; t < tiles; ++t) {
-            __syncthreads();  // the previous tile has been read
-            store_keys(pre);
-            __syncthreads();
-            if (t + 1 < tiles) fetch(a.k, t + 1, wg, pre);
+            if (t + 1 < tiles) issue_keys(t + 1, wg);  // into the other buffer, read two iterations ago
+            tile_ready(t, tiles);
+            const float* buf = tile + (t & 1) * kTileFloats;
 #pragma unroll 1
             for (int m = 0; m < kBlkKeys / 16; ++m) {
                 const int ka = static_cast<int>(warp) + 16 * m, kb = ka + 8;  // this warp's two keys
                 const int wa = t * kBlkKeys + ka;
                 if (wa >= wg) break;
-                const float4* xa = reinterpret_cast<const float4*>(tile + ka * kKeyPitch + j * kJStride);
-                const float4* xb = reinterpret_cast<const float4*>(tile + kb * kKeyPitch + j * kJStride);
+                const float4* xa = reinterpret_cast<const float4*>(buf + ka * kKeyPitch + j * kJStride);
+                const float4* xb = reinterpret_cast<const float4*>(buf + kb * kKeyPitch + j * kJStride);
                 float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;   // (a, combo 0), (a, 1), (b, 0), (b, 1)
 #pragma unroll
                 for (int t4 = 0; t4 < 8; ++t4) {
@@ -379,8 +404,8 @@ struct BlockAttention {
                     }
                 }
             }
+            __syncthreads();  // buffer t & 1 is refilled by the next iteration's issue
         }
-        __syncthreads();
 
         // ---- softmax of every (row, head) over the row's window: warp `warp`
         // takes keys [wg * warp / 8, wg * (warp + 1) / 8), lane (combo c,
@@ -436,48 +461,86 @@ struct BlockAttention {
         }
 
         // ---- out[r][h][d] = sum_w p[w][r * 4 + h] v[w][d], ascending w ----
-        const int rp = static_cast<int>(tid >> 6), dp = static_cast<int>(tid & 63);  // row; d pair
-        const std::size_t prp = p0 + rp;
-        const int plo = static_cast<int>((prp + 1 > a.window ? prp + 1 - a.window : 0) - begin);
-        const int phi = static_cast<int>(prp - begin);
-        float acc[kGroup][2] = {};
-        fetch(a.v, 0, wg, pre);
+        // Threads 0..127: rows ra = 2 * (tid / 64) and ra + 1, dimensions
+        // 2 * (tid % 64) and + 1, all four heads: 16 chains per thread, each
+        // value pair read once for both rows. The deeper row's window is the
+        // shallower one's shifted by at most one key at each end, so each
+        // tile splits into (shallower only) (both) (deeper only) key runs.
+        const bool pv = tid < 128;
+        const int ra = 2 * static_cast<int>(tid >> 6), dp = static_cast<int>(tid & 63);
+        constexpr int kNone = 1 << 30;
+        int loa = kNone, hia = -1, lob = kNone, hib = -1;
+        if (pv && ra < g) {
+            const std::size_t pr = p0 + ra;
+            loa = static_cast<int>((pr + 1 > a.window ? pr + 1 - a.window : 0) - begin);
+            hia = static_cast<int>(pr - begin);
+        }
+        if (pv && ra + 1 < g) {
+            const std::size_t pr = p0 + ra + 1;
+            lob = static_cast<int>((pr + 1 > a.window ? pr + 1 - a.window : 0) - begin);
+            hib = static_cast<int>(pr - begin);
+        }
+        float acc[2][kGroup][2] = {};
+        issue_values(0, wg);  // the key buffers were released by the last QK barrier
         for (int t = 0; t < tiles; ++t) {
-            __syncthreads();  // softmax done / the previous tile has been read
-            store_values(pre);
-            __syncthreads();
-            if (t + 1 < tiles) fetch(a.v, t + 1, wg, pre);
-            if (rp < g) {
-                const int w0 = max(plo - t * kBlkKeys, 0), w1 = min(phi - t * kBlkKeys, kBlkKeys - 1);
-                const float* prow = scores + static_cast<std::size_t>(t * kBlkKeys) * kCombos + 4 * rp;
+            if (t + 1 < tiles) issue_values(t + 1, wg);
+            tile_ready(t, tiles);  // (the first also orders the softmax before PV)
+            const float* buf = tile + (t & 1) * kTileFloats + 2 * dp;
+            if (hia >= 0) {
+                const int tb = t * kBlkKeys;
+                const int w0a = max(loa - tb, 0), w1a = min(hia - tb, kBlkKeys - 1);
+                const int w0b = lob == kNone ? kNone : max(lob - tb, 0), w1b = min(hib - tb, kBlkKeys - 1);
+                const float* prow = scores + static_cast<std::size_t>(tb) * kCombos + 4 * ra;
+                const int e1 = min(w1a, w0b - 1);
+                for (int w = w0a; w <= e1; ++w) {  // shallower row only
+                    const float4 pa = *reinterpret_cast<const float4*>(prow + w * kCombos);
+                    const float2 vv = *reinterpret_cast<const float2*>(buf + w * kKeyPitch);
+                    acc[0][0][0] = __fmaf_rn(pa.x, vv.x, acc[0][0][0]); acc[0][0][1] = __fmaf_rn(pa.x, vv.y, acc[0][0][1]);
+                    acc[0][1][0] = __fmaf_rn(pa.y, vv.x, acc[0][1][0]); acc[0][1][1] = __fmaf_rn(pa.y, vv.y, acc[0][1][1]);
+                    acc[0][2][0] = __fmaf_rn(pa.z, vv.x, acc[0][2][0]); acc[0][2][1] = __fmaf_rn(pa.z, vv.y, acc[0][2][1]);
+                    acc[0][3][0] = __fmaf_rn(pa.w, vv.x, acc[0][3][0]); acc[0][3][1] = __fmaf_rn(pa.w, vv.y, acc[0][3][1]);
+                }
+                const int e2 = min(w1a, w1b);
 #pragma unroll 4
-                for (int w = w0; w <= w1; ++w) {
-                    const float4 pw = *reinterpret_cast<const float4*>(prow + w * kCombos);
-                    const float2 vv = *reinterpret_cast<const float2*>(tile + w * kKeyPitch + 2 * dp);
-                    acc[0][0] = __fmaf_rn(pw.x, vv.x, acc[0][0]);
-                    acc[0][1] = __fmaf_rn(pw.x, vv.y, acc[0][1]);
-                    acc[1][0] = __fmaf_rn(pw.y, vv.x, acc[1][0]);
-                    acc[1][1] = __fmaf_rn(pw.y, vv.y, acc[1][1]);
-                    acc[2][0] = __fmaf_rn(pw.z, vv.x, acc[2][0]);
-                    acc[2][1] = __fmaf_rn(pw.z, vv.y, acc[2][1]);
-                    acc[3][0] = __fmaf_rn(pw.w, vv.x, acc[3][0]);
-                    acc[3][1] = __fmaf_rn(pw.w, vv.y, acc[3][1]);
+                for (int w = max(w0a, w0b); w <= e2; ++w) {  // both rows
+                    const float4 pa = *reinterpret_cast<const float4*>(prow + w * kCombos);
+                    const float4 pb = *reinterpret_cast<const float4*>(prow + w * kCombos + 4);
+                    const float2 vv = *reinterpret_cast<const float2*>(buf + w * kKeyPitch);
+                    acc[0][0][0] = __fmaf_rn(pa.x, vv.x, acc[0][0][0]); acc[0][0][1] = __fmaf_rn(pa.x, vv.y, acc[0][0][1]);
+                    acc[0][1][0] = __fmaf_rn(pa.y, vv.x, acc[0][1][0]); acc[0][1][1] = __fmaf_rn(pa.y, vv.y, acc[0][1][1]);
+                    acc[0][2][0] = __fmaf_rn(pa.z, vv.x, acc[0][2][0]); acc[0][2][1] = __fmaf_rn(pa.z, vv.y, acc[0][2][1]);
+                    acc[0][3][0] = __fmaf_rn(pa.w, vv.x, acc[0][3][0]); acc[0][3][1] = __fmaf_rn(pa.w, vv.y, acc[0][3][1]);
+                    acc[1][0][0] = __fmaf_rn(pb.x, vv.x, acc[1][0][0]); acc[1][0][1] = __fmaf_rn(pb.x, vv.y, acc[1][0][1]);
+                    acc[1][1][0] = __fmaf_rn(pb.y, vv.x, acc[1][1][0]); acc[1][1][1] = __fmaf_rn(pb.y, vv.y, acc[1][1][1]);
+                    acc[1][2][0] = __fmaf_rn(pb.z, vv.x, acc[1][2][0]); acc[1][2][1] = __fmaf_rn(pb.z, vv.y, acc[1][2][1]);
+                    acc[1][3][0] = __fmaf_rn(pb.w, vv.x, acc[1][3][0]); acc[1][3][1] = __fmaf_rn(pb.w, vv.y, acc[1][3][1]);
+                }
+                for (int w = max(w1a + 1, w0b); w <= w1b; ++w) {  // deeper row only
+                    const float4 pb = *reinterpret_cast<const float4*>(prow + w * kCombos + 4);
+                    const float2 vv = *reinterpret_cast<const float2*>(buf + w * kKeyPitch);
+                    acc[1][0][0] = __fmaf_rn(pb.x, vv.x, acc[1][0][0]); acc[1][0][1] = __fmaf_rn(pb.x, vv.y, acc[1][0][1]);
+                    acc[1][1][0] = __fmaf_rn(pb.y, vv.x, acc[1][1][0]); acc[1][1][1] = __fmaf_rn(pb.y, vv.y, acc[1][1][1]);
+                    acc[1][2][0] = __fmaf_rn(pb.z, vv.x, acc[1][2][0]); acc[1][2][1] = __fmaf_rn(pb.z, vv.y, acc[1][2][1]);
+                    acc[1][3][0] = __fmaf_rn(pb.w, vv.x, acc[1][3][0]); acc[1][3][1] = __fmaf_rn(pb.w, vv.y, acc[1][3][1]);
                 }
             }
+            __syncthreads();  // buffer t & 1 is refilled next
         }
-        if (rp < g) {
-            float* o = a.out + ((first + rp) * a.q_heads + kh * kGroup) * 128 + 2 * dp;
 #pragma unroll
-            for (int h = 0; h < kGroup; ++h)
-                *reinterpret_cast<float2*>(o + h * 128) = make_float2(acc[h][0], acc[h][1]);
-        }
+        for (int rr = 0; rr < 2; ++rr)
+            if (pv && ra + rr < g) {
+                float* o = a.out + ((first + ra + rr) * a.q_heads + kh * kGroup) * 128 + 2 * dp;
+#pragma unroll
+                for (int h = 0; h < kGroup; ++h)
+                    *reinterpret_cast<float2*>(o + h * 128) = make_float2(acc[rr][h][0], acc[rr][h][1]);
+            }
         __syncthreads();  // scores / chain / tile are reused by the next group
         return true;
     }
 };
 
 template <bool EXACT>
-__global__ void __launch_bounds__(kBlkThreads, 1)
+__global__ void __launch_bounds__(kBlkThreads, 2)
 attention_tree_block(AttnArgs a, std::size_t wcap) {
     pdl_begin();
     extern __shared__ __align__(16) float smem[];

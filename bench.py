@@ -421,6 +421,18 @@ def run_config(args) -> dict:
             pipe.run()
         bpr = prefill.bytes_per_row(1)
         nbytes = bpr["total"] * batch.rows
+        # the attention core on the same trie rows, timed on its own (FP32
+        # CUDA-core roofline): q [rows, 16, 128], k and v [rows, 4, 128]
+        trie = ops.prefix_trie(prompts, with_ancestors=True)
+        att_q, att_k, att_v = rn(batch.rows, 2048), rn(batch.rows, 512), rn(batch.rows, 512)
+        att_o = torch.empty_like(att_q)
+        att_pos = torch.from_numpy(trie.node_depth.view(np.int32)).to(dev)
+        att_anc = torch.from_numpy(trie.node_anc.view(np.int32)).to(dev)
+        att_keys = int(np.minimum(trie.node_depth + 1, ops.SLIDING_WINDOW).sum())
+
+        def attention():
+            ops.attention_tree_gpu(att_q, att_k, att_v, att_o, att_pos, att_anc, trie.anc_stride, batch.rows, 16, 4,
+                                   128, ops.SLIDING_WINDOW, exact=args.exact)
         work = (f"config 4: one layer's non-GEMM path, 16 prompts x 1024 tokens with a 256-token shared prefix "
                 f"({batch.rows} trie rows)")
         tokens = batch.tokens
@@ -435,6 +447,25 @@ def run_config(args) -> dict:
             b_.record()
         torch.cuda.synchronize()
     ms = statistics.median(a.elapsed_time(b_) for a, b_ in ev)
+    att = None
+    if cfg == 4:
+        attention()
+        aev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(max(3, args.steps // 4))]
+        for a, b_ in aev:
+            flush.zero_()
+            a.record()
+            attention()
+            b_.record()
+        torch.cuda.synchronize()
+        att_ms = statistics.median(a.elapsed_time(b_) for a, b_ in aev)
+        flops = 2 * 2 * 16 * 128 * att_keys  # QK and PV multiply-adds over every (row, head, key)
+        fp32_peak = 148 * 128 * 2 * 1965e6 / 1e12
+        att = {"kernel": "attention_tree_block", "ms": round(att_ms, 4), "flops": flops,
+               "achieved": round(flops / (att_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "bound": "fp32",
+               "peak": round(fp32_peak, 1), "frac": round(flops / (att_ms * 1e-3) / 1e12 / fp32_peak, 3),
+               "peak_kind": "nominal FP32 CUDA-core rate (148 SMs x 128 lanes x 2 flops x 1965 MHz); "
+                            "MEASURED_PEAKS.json has no FP32 figure"}
     peak, peak_kind = peaks()
     gbs = nbytes / (ms * 1e-3) / 1e9
     res = {"metric": f"config {cfg} " + ("non-GEMM tokens/s" if cfg == 4 else "algorithmic HBM GB/s"),
@@ -447,6 +478,8 @@ def run_config(args) -> dict:
            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(gbs / peak, 3), "peak_kind": peak_kind, "traffic": None},
            "clocks": {k: v for k, v in clocks.summary().items() if k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+    if att:
+        res["attention_core"] = att
     return res
 
 
