@@ -91,3 +91,9 @@ extern "C" int b2_gather_rows(const float* x, size_t x_rows, size_t h,
     }
     return launch_result("b2_gather_rows");
 }
+
+extern "C" int b2_moe_gather_compact(const float* x, size_t x_rows, size_t h,
+                                     const uint32_t* assignment_rows, size_t assignments,
+                                     float* compact, b2_stream_t stream) {
+    return b2_gather_rows(x, x_rows, h, assignment_rows, assignments, compact, stream);
+}

@@ -100,6 +100,17 @@ def gather_rows_gpu(x: torch.Tensor, rows, out: torch.Tensor) -> None:
            "gather_rows_gpu")
 
 
+def moe_gather_compact_gpu(x: torch.Tensor, assignment_rows: torch.Tensor, out: torch.Tensor) -> None:
+    """out[i, :] = x[assignment_rows[i], :], the expert-ordered input of the
+    grouped expert GEMM (k_moe_gather_compact, src/tensor.cu:1420-1428)."""
+    x_rows, h = _rows_h(x)
+    count = assignment_rows.numel()
+    if out.numel() != count * h:
+        raise InvalidArgument("moe_gather_compact shape")
+    _check(_lib.lib().b2_moe_gather_compact(_f32(x), x_rows, h, _u32(assignment_rows), count, _f32(out), _stream()),
+           "moe_gather_compact_gpu")
+
+
 # ---- LayerNorm ------------------------------------------------------------------
 
 

@@ -88,6 +88,17 @@ int b2_gather_rows(const float* x, size_t x_rows, size_t h,
                    const uint32_t* rows, size_t count, float* out,
                    b2_stream_t stream);
 
+/*
+ * The MoE permutation gather: compact[i, :] = x[assignment_rows[i], :] for
+ * i < assignments (2T), the expert-ordered GEMM input. Replaces
+ * k_moe_gather_compact (src/tensor.cu:1420-1428) as moe_forward_grouped_gpu
+ * launches it when the gather is not fused into its GEMM (:2824-2833).
+ * The same kernel as b2_gather_rows (one CTA per row, 128-bit copies).
+ */
+int b2_moe_gather_compact(const float* x, size_t x_rows, size_t h,
+                          const uint32_t* assignment_rows, size_t assignments,
+                          float* compact, b2_stream_t stream);
+
 /* ---- LayerNorm ------------------------------------------------------------ */
 
 /*

@@ -131,6 +131,15 @@ int ref_k_moe_combine(const float* expert_out, const std::uint8_t* routes,
     return launch_status();
 }
 
+// k_moe_gather_compact with the launch of moe_forward_grouped_gpu
+// (src/tensor.cu:1420-1428, :2828-2833): compact[i,:] = x[assignment_rows[i],:].
+int ref_k_moe_gather_compact(const float* x, const std::uint32_t* assignment_rows, float* out,
+                             std::size_t assignments, std::size_t h, void* stream) {
+    tensor_ops::k_moe_gather_compact<<<blocks_for(assignments * h), 256, 0, as_stream(stream)>>>(
+        x, assignment_rows, out, assignments, h);
+    return launch_status();
+}
+
 int ref_k_add(float* a, const float* b, std::size_t n, void* stream) {
     tensor_ops::k_add<<<blocks_for(n), 256, 0, as_stream(stream)>>>(a, b, n);
     return launch_status();

@@ -251,3 +251,25 @@ def test_ref_softmax_via_attention(ops, cuda, T):
             oracle.assert_bitexact(to_host(probs), np.ascontiguousarray(ref_p), "b2 exact vs ref softmax")
         else:
             oracle.assert_close(to_host(probs), ref_p, what="b2 vs ref softmax")
+
+
+def test_ref_moe_gather_compact(ops, cuda):
+    """The permutation gather with the assignment rows of a real routing, vs
+    the reference's k_moe_gather_compact and the oracle, bit for bit."""
+    import torch
+
+    g = rng(27)
+    T, h = 3000, 4096
+    x = normal(g, (T, h))
+    logits = normal(g, (T, 16))
+    r = oracle.moe_route(logits)
+    arows = r["assignment_rows"]
+    xd, ad = to_dev(x, cuda), to_dev(arows, cuda)
+    ref = torch.full((2 * T, h), float("nan"), device=cuda)
+    _run(oracle.ref().ref_k_moe_gather_compact(xd.data_ptr(), ad.data_ptr(), ref.data_ptr(), 2 * T, h, _stream()))
+    got = torch.full_like(ref, float("nan"))
+    ops.moe_gather_compact_gpu(xd, ad, got)
+    torch.cuda.synchronize()
+    want = oracle.gather_rows(x, arows)
+    oracle.assert_bitexact(to_host(ref), want, "oracle vs reference gather_compact")
+    oracle.assert_bitexact(to_host(got), want, "b2 vs reference gather_compact")
