@@ -142,3 +142,38 @@ def test_chunk_plan_fractions():
     assert any({0, 1} <= set(p) for p in plan[0])
     with pytest.raises(ValueError):
         chunk_plan(prompts, 2, 3, (0.5, 0.5))
+
+
+def _rank_with_failed_peer(rank, world, port, out_path):
+    """Rank 1 'fails' (exits without cleanup) before its gather; rank 0's
+    gather must end with an error, not wait forever."""
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(0)
+    t0 = time.monotonic()
+    send = torch.zeros(4, 8)
+    recv = [torch.empty_like(send) for _ in range(world)]
+    try:
+        dist.gather(send, recv, dst=0)
+        status = "no error"
+    except Exception as e:  # noqa: BLE001 -- any error type counts as detection
+        status = "error " + type(e).__name__
+    with open(out_path, "w") as f:
+        f.write(f"{status}\n{time.monotonic() - t0:.1f}\n")
+    os._exit(0)  # a group with a dead peer cannot be torn down cleanly
+
+
+def test_failed_rank_is_detected_by_the_gather(tmp_path):
+    out = str(tmp_path / "status.txt")
+    mp.start_processes(_rank_with_failed_peer, args=(2, _free_port(), out), nprocs=2, join=True,
+                       start_method="spawn")
+    status, seconds = open(out).read().split("\n")[:2]
+    assert status.startswith("error"), status
+    assert float(seconds) < 60.0
