@@ -253,20 +253,6 @@ inline std::size_t block_smem_bytes(std::size_t wcap) {
     return (wcap * kCombos + wcap + 2 * static_cast<std::size_t>(kTileFloats)) * 4;
 }
 
-// Asynchronous global -> shared copies (no registers held while in flight).
-__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(
-                     static_cast<unsigned>(__cvta_generic_to_shared(dst))), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(
-                     static_cast<unsigned>(__cvta_generic_to_shared(dst))), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
 template <bool EXACT>
 struct BlockAttention {

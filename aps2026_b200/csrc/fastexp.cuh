@@ -33,7 +33,9 @@ __device__ __forceinline__ void load_exp2_table(double* smem64) {
     for (int i = threadIdx.x; i < 64; i += blockDim.x) smem64[i] = kExp2Table[i];
 }
 
-__device__ __forceinline__ float exp_ref_slow(float x) {
+// Out of line: each kernel inlines exp_ref many times, and the rare slow
+// path inlined at every site would multiply the code size.
+static __device__ __noinline__ float exp_ref_slow(float x) {
     return static_cast<float>(exp(static_cast<double>(x)));
 }
 
@@ -43,12 +45,11 @@ __device__ __forceinline__ float exp_ref_slow(float x) {
 // subnormal) or NaN, or y within the error bound of a float rounding
 // midpoint. The returned value is meaningless when *slow is set.
 //
-// Conversions are kept off the quarter-rate conversion pipe: n comes from
-// the low word of x * 64/ln2 + 1.5 * 2^52 (round to nearest integer by the
-// addition itself), and the final rounding of y to float is done on its bit
-// pattern (the near-midpoint case being excluded, rounding is "round half
-// up" on the 29 dropped bits, and the carry runs into the exponent field
-// exactly as the next float up).
+// n comes from the low word of x * 64/ln2 + 1.5 * 2^52 (round to nearest
+// integer by the addition itself); 2^m is applied by adding m to the
+// exponent field of y (y * 2^m stays a normal double), and one
+// round-to-nearest conversion gives the float (a normal float for |x| <= 80;
+// ties are among the near-midpoint cases sent to the slow path).
 __device__ __forceinline__ float exp_ref_fast(float x, const double* tab, bool* slow) {
     const bool out_of_range = !(fabsf(x) <= 80.0f);     // also NaN
     const double xd = static_cast<double>(out_of_range ? 0.0f : x);
@@ -65,24 +66,23 @@ __device__ __forceinline__ float exp_ref_fast(float x, const double* tab, bool* 
     p *= r;                                             // e^r - 1
     const double t = tab[j];
     const double y = fma(t, p, t);                      // 2^(j/64) e^r, in [0.99, 2)
-    const unsigned lo = static_cast<unsigned>(__double2loint(y));
-    const unsigned hi = static_cast<unsigned>(__double2hiint(y));
-    const int low29 = static_cast<int>(lo & 0x1FFFFFFFu);
+    const int lo = __double2loint(y);
+    const int low29 = lo & 0x1FFFFFFF;
     *slow = out_of_range | (abs(low29 - 0x10000000) < 2048);
-    // float bits of y * 2^m: exponent (biased 1023 -> 127, plus m), the top
-    // 23 of the 52 significand bits, plus one when the dropped bits exceed half
-    const unsigned bits = ((((hi >> 20) - 896u) + static_cast<unsigned>(m)) << 23) |
-                          ((hi & 0xFFFFFu) << 3) | (lo >> 29);
-    return __uint_as_float(bits + (low29 > 0x10000000 ? 1u : 0u));
+    const int hi = __double2hiint(y) + static_cast<int>(static_cast<unsigned>(m) << 20);  // y * 2^m
+    return __double2float_rn(__hiloint2double(hi, lo));
 }
 
 // Returns (float)exp((double)x); `tab` is the shared table. `slow`, when
-// given, is set when the call took the exp(double) path.
+// given, is set when the call took the exp(double) path. Below -104 the
+// result is +0 without calling it: e^-104 = 6.8e-46 is under half the
+// smallest float subnormal (2^-150 = 7.0e-46), so it rounds to zero (this
+// also makes -inf, a masked score, cheap).
 __device__ __forceinline__ float exp_ref(float x, const double* tab, bool* slow = nullptr) {
     bool s;
     const float f = exp_ref_fast(x, tab, &s);
     if (slow) *slow = s;
-    return s ? exp_ref_slow(x) : f;
+    return s ? (x < -104.0f ? 0.0f : exp_ref_slow(x)) : f;
 }
 
 }  // namespace b2

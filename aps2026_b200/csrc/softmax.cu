@@ -44,11 +44,84 @@ struct SoftmaxArgs {
 // FMA-pipe operations instead of a full division per element; arguments
 // below 2^-96, whose residual could leave the normal range, divide directly.
 __device__ __forceinline__ float div_by_row(float e, float d, float y) {
-    if (e < 0x1p-96f) return __fdiv_rn(e, d);
+    if (e < 0x1p-96f) return e == 0.0f ? 0.0f : __fdiv_rn(e, d);
     const float q = __fmul_rn(e, y);
     const float r = __fmaf_rn(-d, q, e);
     return __fmaf_rn(r, y, q);
 }
+
+// The part of one row a thread holds: V chunks of 4 keys, chunk k at keys
+// 4 c_k .. 4 c_k + 3 with c_k = first + k * stride. Chunks with no key in
+// the window [begin, i] are never read; inside read chunks, keys outside the
+// window hold -inf, whose exponential is +0 (no per-element masks in the
+// exponential or sum).
+template <int V>
+struct RowPart {
+    float v[V][4];
+    unsigned any = 0, full = 0;  // bit k: chunk k holds some / only window keys
+
+    // Loads and scales the chunks; returns the thread's max score.
+    __device__ __forceinline__ float load(const float4* src, std::size_t first, std::size_t stride,
+                                          std::size_t T4, std::size_t begin, std::size_t i, float scale) {
+        float mx = -3.402823466e+38F;
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+            const std::size_t c = first + static_cast<std::size_t>(k) * stride, j0 = 4 * c;
+            const bool a_k = c < T4 && j0 <= i && j0 + 3 >= begin;
+            const bool f_k = a_k && j0 >= begin && j0 + 3 <= i;
+            any |= static_cast<unsigned>(a_k) << k;
+            full |= static_cast<unsigned>(f_k) << k;
+            const float4 s = a_k ? ld_stream(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[k][0] = __fmul_rn(s.x, scale);
+            v[k][1] = __fmul_rn(s.y, scale);
+            v[k][2] = __fmul_rn(s.z, scale);
+            v[k][3] = __fmul_rn(s.w, scale);
+            if (!f_k) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (!(a_k && j0 + e >= begin && j0 + e <= i)) v[k][e] = -__int_as_float(0x7f800000);
+            }
+            mx = fmaxf(mx, fmaxf(fmaxf(v[k][0], v[k][1]), fmaxf(v[k][2], v[k][3])));
+        }
+        return mx;
+    }
+    // v <- exp(v - m) (zeros in unread chunks); returns the thread's sum.
+    __device__ __forceinline__ float exp_sum(float m, const double* tab) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+            if ((any >> k) & 1u) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    v[k][e] = exp_ref(__fsub_rn(v[k][e], m), tab);
+                    sum = __fadd_rn(sum, v[k][e]);
+                }
+            } else {
+                v[k][0] = v[k][1] = v[k][2] = v[k][3] = 0.0f;
+            }
+        }
+        return sum;
+    }
+    // dst chunk c_k <- v / d (zeros outside the window).
+    __device__ __forceinline__ void store(float4* dst, std::size_t first, std::size_t stride, std::size_t T4,
+                                          std::size_t begin, std::size_t i, float d, float y) const {
+#pragma unroll
+        for (int k = 0; k < V; ++k) {
+            const std::size_t c = first + static_cast<std::size_t>(k) * stride, j0 = 4 * c;
+            if (c >= T4) continue;
+            float pv[4] = {0.f, 0.f, 0.f, 0.f};
+            if ((full >> k) & 1u) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) pv[e] = div_by_row(v[k][e], d, y);
+            } else if ((any >> k) & 1u) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (j0 + e >= begin && j0 + e <= i) pv[e] = div_by_row(v[k][e], d, y);
+            }
+            st_plain(dst + c, make_float4(pv[0], pv[1], pv[2], pv[3]));
+        }
+    }
+};
 
 // One CTA of THREADS threads per query row, V float4 per thread; block
 // reductions through shared memory.
@@ -69,43 +142,17 @@ causal_softmax_block(SoftmaxArgs a) {
         const std::size_t begin = i + 1 > a.window ? i + 1 - a.window : 0;
         const float4* src = reinterpret_cast<const float4*>(a.scores + row * a.ld);
         float4* dst = reinterpret_cast<float4*>(a.probs + row * a.ld);
-        float v[V][4];
-        unsigned valid = 0;  // bit 4k+e: element e of chunk k is inside the window
-        float local_max = -3.402823466e+38F;
-#pragma unroll
-        for (int k = 0; k < V; ++k) {
-            const std::size_t c = threadIdx.x + static_cast<std::size_t>(k) * THREADS;
-            const std::size_t j0 = 4 * c;
-            const bool any = c < T4 && j0 <= i && j0 + 3 >= begin;
-            float4 s = any ? ld_stream(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float sv[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const std::size_t j = j0 + e;
-                v[k][e] = __fmul_rn(sv[e], a.scale);
-                if (any && j >= begin && j <= i) {
-                    valid |= 1u << (4 * k + e);
-                    local_max = fmaxf(local_max, v[k][e]);
-                }
-            }
-        }
-        const float m = block_max<WARPS>(local_max, red[0]);
-        float local_sum = 0.0f;
-#pragma unroll
-        for (int k = 0; k < V; ++k)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float ex = (valid >> (4 * k + e)) & 1u ? exp_ref(__fsub_rn(v[k][e], m), tab) : 0.0f;
-                v[k][e] = ex;
-                local_sum = __fadd_rn(local_sum, ex);
-            }
+        RowPart<V> part;
+        const float m = block_max<WARPS>(part.load(src, threadIdx.x, THREADS, T4, begin, i, a.scale), red[0]);
+        const float local_sum = part.exp_sum(m, tab);
         float denom;
         if (EXACT) {
 #pragma unroll
             for (int k = 0; k < V; ++k) {
                 const std::size_t c = threadIdx.x + static_cast<std::size_t>(k) * THREADS;
                 if (c < T4)
-                    reinterpret_cast<float4*>(staged)[c] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
+                    reinterpret_cast<float4*>(staged)[c] =
+                        make_float4(part.v[k][0], part.v[k][1], part.v[k][2], part.v[k][3]);
             }
             __syncthreads();
             if (threadIdx.x == 0) {
@@ -118,18 +165,7 @@ causal_softmax_block(SoftmaxArgs a) {
         } else {
             denom = block_sum<WARPS>(local_sum, red[1]);
         }
-        const float rden = __frcp_rn(denom);
-#pragma unroll
-        for (int k = 0; k < V; ++k) {
-            const std::size_t c = threadIdx.x + static_cast<std::size_t>(k) * THREADS;
-            if (c < T4) {
-                float pv[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    pv[e] = (valid >> (4 * k + e)) & 1u ? div_by_row(v[k][e], denom, rden) : 0.0f;
-                st_plain(dst + c, make_float4(pv[0], pv[1], pv[2], pv[3]));
-            }
-        }
+        part.store(dst, threadIdx.x, THREADS, T4, begin, i, denom, __frcp_rn(denom));
         if (EXACT) __syncthreads();  // staged[] / denom_s reused by the next row
     }
 }
@@ -160,42 +196,17 @@ causal_softmax_warp(SoftmaxArgs a) {
         const std::size_t begin = i + 1 > a.window ? i + 1 - a.window : 0;
         const float4* src = reinterpret_cast<const float4*>(a.scores + row * a.ld);
         float4* dst = reinterpret_cast<float4*>(a.probs + row * a.ld);
-        float v[V][4];
-        unsigned long long valid = 0;  // bit 4k+e: element e of chunk k is inside the window
-        float local_max = -3.402823466e+38F;
-#pragma unroll
-        for (int k = 0; k < V; ++k) {
-            const std::size_t c = lane + 32 * static_cast<std::size_t>(k);
-            const std::size_t j0 = 4 * c;
-            const bool any = c < T4 && j0 <= i && j0 + 3 >= begin;
-            const float4 sv = any ? ld_stream(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const std::size_t j = j0 + e;
-                v[k][e] = __fmul_rn(s4[e], a.scale);
-                if (any && j >= begin && j <= i) {
-                    valid |= 1ull << (4 * k + e);
-                    local_max = fmaxf(local_max, v[k][e]);
-                }
-            }
-        }
-        const float m = warp_max(local_max);
-        float local_sum = 0.0f;
-#pragma unroll
-        for (int k = 0; k < V; ++k)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float ex = (valid >> (4 * k + e)) & 1ull ? exp_ref(__fsub_rn(v[k][e], m), tab) : 0.0f;
-                v[k][e] = ex;
-                local_sum = __fadd_rn(local_sum, ex);
-            }
+        RowPart<V> part;
+        const float m = warp_max(part.load(src, lane, 32, T4, begin, i, a.scale));
+        const float local_sum = part.exp_sum(m, tab);
         float denom;
         if (EXACT) {
 #pragma unroll
             for (int k = 0; k < V; ++k) {
                 const std::size_t c = lane + 32 * static_cast<std::size_t>(k);
-                if (c < T4) reinterpret_cast<float4*>(mine)[c] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
+                if (c < T4)
+                    reinterpret_cast<float4*>(mine)[c] =
+                        make_float4(part.v[k][0], part.v[k][1], part.v[k][2], part.v[k][3]);
             }
             __syncwarp();
             float d = 0.0f;
@@ -205,18 +216,7 @@ causal_softmax_warp(SoftmaxArgs a) {
         } else {
             denom = warp_sum(local_sum);
         }
-        const float rden = __frcp_rn(denom);
-#pragma unroll
-        for (int k = 0; k < V; ++k) {
-            const std::size_t c = lane + 32 * static_cast<std::size_t>(k);
-            if (c < T4) {
-                float pv[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    pv[e] = (valid >> (4 * k + e)) & 1ull ? div_by_row(v[k][e], denom, rden) : 0.0f;
-                st_plain(dst + c, make_float4(pv[0], pv[1], pv[2], pv[3]));
-            }
-        }
+        part.store(dst, lane, 32, T4, begin, i, denom, __frcp_rn(denom));
         if (EXACT) __syncwarp();  // the warp's staging slice is reused by its next row
     }
 }

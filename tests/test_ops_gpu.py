@@ -330,7 +330,8 @@ def test_fast_exp_matches_exp_double_on_every_float(ops, cuda):
     total = mism = slow = 0
     for lo, hi in [(0, bits(80.0) + 1), (0x80000000, bits(-80.0) + 1),     # every float with |x| <= 80
                    (bits(80.0) + 1, bits(200.0)), (bits(-80.0) + 1, bits(-200.0)),
-                   (0x7F800000, 0x7F800001 + 16)]:                         # inf and NaNs
+                   (bits(-200.0), 0xFF800001),                             # every float below -200, and -inf
+                   (0x7F800000, 0x7F800001 + 16), (0xFF800001, 0xFF800001 + 16)]:  # +inf and NaNs
         c, m, s = run(lo, hi)
         total, mism, slow = total + c, mism + m, slow + s
     assert total > 2_200_000_000
