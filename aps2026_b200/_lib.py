@@ -35,6 +35,8 @@ SIGNATURES: dict[str, tuple] = {
     "b2_device_status": (C.c_int, [_vp, _vp]),
     "b2_gather_rows": (C.c_int, [_vp, _sz, _sz, _vp, _sz, _vp, _vp]),
     "b2_moe_gather_compact": (C.c_int, [_vp, _sz, _sz, _vp, _sz, _vp, _vp]),
+    "b2_prefix_trie_device_workspace_size": (C.c_int, [_sz, _vp]),
+    "b2_prefix_trie_device": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "b2_layer_norm": (C.c_int, [_vp, _vp, _vp, _vp, _sz, _sz, _f32, _u32, _vp]),
     "b2_add_layer_norm": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _f32, _u32, _vp]),
     "b2_moe_combine_add_layer_norm": (

@@ -361,3 +361,43 @@ def prefix_trie(prompts: Sequence[Sequence[int]], vocab: int = 32064, max_len: i
     return PrefixTrie(token_node, node_token[:n].copy(), node_depth[:n].copy(),
                       anc[: n * stride].reshape(n, stride).copy() if anc is not None else None,
                       stride, n)
+
+
+@dataclass
+class DeviceTrie:
+    """Outputs of b2_prefix_trie_device (int32 device tensors)."""
+    token_node: torch.Tensor   # [total]
+    node_token: torch.Tensor   # [nodes]
+    node_depth: torch.Tensor   # [nodes]
+    node_prompt: torch.Tensor  # [nodes]: a prompt containing the node
+    nodes: int
+
+
+class TrieWorkspace:
+    """Caller-owned scratch of b2_prefix_trie_device."""
+
+    def __init__(self, batch: int, device):
+        n = C.c_size_t(0)
+        _check(_lib.lib().b2_prefix_trie_device_workspace_size(batch, C.addressof(n)), "workspace size")
+        self.bytes = n.value
+        self.buf = torch.empty(max(1, (self.bytes + 3) // 4), dtype=torch.int32, device=device)
+
+
+def prefix_trie_device(ids: torch.Tensor, offsets: torch.Tensor, vocab: int = 32064, max_len: int = 4096,
+                       ws: "TrieWorkspace | None" = None) -> DeviceTrie:
+    """The prefix trie of the prompts ids[offsets[b]:offsets[b+1]] (int32
+    device tensors) built on the GPU and numbered as PhiTinyMoEModel::generate
+    numbers it (src/model.cu:64-117); reads the node count back (a 4-byte
+    copy, which waits for the build)."""
+    batch, total = offsets.numel() - 1, ids.numel()
+    if batch < 1:
+        raise InvalidArgument("generate received an empty input batch")
+    dev = ids.device
+    e = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=dev)  # noqa: E731
+    token_node, node_token, node_depth, node_prompt, count = e(total), e(total), e(total), e(total), e(1)
+    ws = ws or TrieWorkspace(batch, dev)
+    _check(_lib.lib().b2_prefix_trie_device(_u32(ids), _u32(offsets), batch, total, vocab, max_len, _u32(token_node),
+                                            _u32(node_token), _u32(node_depth), _u32(node_prompt), _u32(count),
+                                            ws.buf.data_ptr(), ws.bytes, _stream()), "prefix_trie_device")
+    n = int(count[0].item())
+    return DeviceTrie(token_node[:total], node_token[:n], node_depth[:n], node_prompt[:n], n)

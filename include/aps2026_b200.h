@@ -73,6 +73,7 @@ const char* b2_last_error(void);
 #define B2_CHECK_ROPE 2u
 #define B2_CHECK_COMBINE 4u
 #define B2_CHECK_ATTENTION 8u
+#define B2_CHECK_TRIE 16u
 int b2_device_status(uint32_t* status_out, b2_stream_t stream);
 
 /* ---- embedding / row gather ---------------------------------------------- */
@@ -286,7 +287,7 @@ int b2_moe_combine(const float* expert_out, size_t expert_rows,
  */
 int b2_add(float* a, const float* b, size_t n, b2_stream_t stream);
 
-/* ---- prefix-trie dedup (host) --------------------------------------------- */
+/* ---- prefix-trie dedup ------------------------------------------------------ */
 
 /*
  * HOST function. Builds the prefix trie of `batch` prompts packed in `ids`
@@ -308,6 +309,36 @@ int b2_prefix_trie_build(const int32_t* ids, const uint32_t* seq_lens,
                          uint32_t* token_node, uint32_t* node_token,
                          uint32_t* node_depth, uint32_t* node_anc,
                          size_t anc_stride, size_t* nodes_out);
+
+/*
+ * DEVICE twin of b2_prefix_trie_build, no reference counterpart as a kernel
+ * (the reference walks the trie on the host, src/model.cu:64-117): the same
+ * token_node / node_token / node_depth, numbered identically, computed from
+ * longest common prefixes with earlier prompts on the GPU, so an end-to-end
+ * step uploads token ids only. All pointers are device memory:
+ *   ids        [total]      int32 token ids, prompts packed back to back
+ *   offsets    [batch + 1]  prompt b is ids[offsets[b] .. offsets[b + 1]),
+ *                           offsets[0] = 0, offsets[batch] = total
+ *   token_node [total]; node_token, node_depth [total] (the first
+ *   *node_count entries are written); node_prompt [total] or NULL: a prompt
+ *   containing each node, so its ancestor chain root..node is
+ *   token_node[offsets[p] .. offsets[p] + node_depth[node]] (the compact form
+ *   of node_anc); node_count: device uint32 scalar.
+ * Workspace: b2_prefix_trie_device_workspace_size bytes, 4-byte aligned.
+ * Inputs the host version rejects (an empty or over-long prompt, a token
+ * outside [0, vocab), offsets that do not split [0, total)) are reported
+ * through b2_device_status (B2_CHECK_TRIE); no access leaves the arrays.
+ * Cost: O(batch^2) prefix comparisons (one 32-token step for unrelated
+ * prompts) plus O(total).
+ */
+int b2_prefix_trie_device_workspace_size(size_t batch, size_t* bytes);
+int b2_prefix_trie_device(const int32_t* ids, const uint32_t* offsets,
+                          size_t batch, size_t total, size_t vocab,
+                          size_t max_len, uint32_t* token_node,
+                          uint32_t* node_token, uint32_t* node_depth,
+                          uint32_t* node_prompt, uint32_t* node_count,
+                          void* workspace, size_t workspace_bytes,
+                          b2_stream_t stream);
 
 /* ---- diagnostics --------------------------------------------------------------- */
 
