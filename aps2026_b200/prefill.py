@@ -136,20 +136,14 @@ class Batch:
     """A prompt batch deduplicated onto prefix-trie nodes, with its index
     arrays on the device."""
     prompts: list
-    trie: ops.PrefixTrie
+    trie: "ops.PrefixTrie | None"  # the host trie; None when it was built on the device
     node_token: torch.Tensor    # int32 [nodes] on device
     node_depth: torch.Tensor    # int32 [nodes]
     token_node: torch.Tensor    # int32 [tokens]
     last_rows: torch.Tensor     # int32 [batch]: node of each prompt's last token
     max_len: int
-
-    @property
-    def rows(self) -> int:
-        return self.trie.nodes
-
-    @property
-    def tokens(self) -> int:
-        return int(self.trie.token_node.size)
+    rows: int                   # trie nodes
+    tokens: int
 
     @staticmethod
     def build(prompts: Sequence[np.ndarray], device, pinned: bool = False, stream=None) -> "Batch":
@@ -165,7 +159,7 @@ class Batch:
             return t.to(device, non_blocking=pinned)
 
         return Batch(list(prompts), trie, up(trie.node_token), up(trie.node_depth), up(trie.token_node),
-                     up(last), int(lens.max()))
+                     up(last), int(lens.max()), trie.nodes, int(lens.sum()))
 
 
 class Pipeline:
@@ -242,9 +236,10 @@ class Pipeline:
 
 def identity_rows(batch: Batch) -> bool:
     """True when every token row is its own trie node in order (no shared
-    prefixes): the final node rows are then already the token rows."""
-    tn = batch.trie.token_node
-    return batch.rows == tn.size and bool((tn == np.arange(tn.size, dtype=tn.dtype)).all())
+    prefixes): the final node rows are then already the token rows. (With as
+    many nodes as tokens every token creates its node, and creation order is
+    token order.)"""
+    return batch.rows == batch.tokens
 
 
 def slice_standins(s: StandIns, r0: int, rows: int) -> StandIns:
@@ -255,40 +250,77 @@ def slice_standins(s: StandIns, r0: int, rows: int) -> StandIns:
 
 
 class HostStage:
-    """Uploads a chunk's trie index arrays for an end-to-end step: one
-    pinned host buffer per chunk (two, used alternately, so filling one never
-    waits for the copy out of the other), reused across steps, and one
-    asynchronous copy per chunk into a device buffer on the current stream."""
+    """The host side of an end-to-end step: takes a chunk's prompts as host
+    token ids and makes its Batch on the device.
 
-    def __init__(self, device, batches: Sequence["Batch"]):
-        """Sizes the pinned buffers for `batches` (allocating pinned memory
-        inside a timed loop would stall it)."""
-        self.device = device
-        n = [2 * b.rows + b.tokens + len(b.prompts) for b in batches]
-        self.host = [[torch.empty(k, dtype=torch.int32, pin_memory=True) for k in n] for _ in range(2)]
-        self.done = [[None] * len(batches) for _ in range(2)]
+    Device mode (default): packs [offsets | ids] into a pinned buffer, copies
+    it up asynchronously and builds the trie on the GPU
+    (b2_prefix_trie_device) on a high-priority stream of its own, so the
+    build overlaps the previous step still running; only the node count
+    comes back (the host needs it to size the launches). Host mode: builds
+    the trie on the host (b2_prefix_trie_build) and copies its index arrays
+    up on the current stream.
+
+    Every buffer exists twice and alternates by step, so preparing step k + 1
+    waits only for step k - 1 (mark_used() records when a step is done with
+    its buffers); all buffers are sized once, for the batches given
+    (allocating pinned memory inside a timed loop would stall it)."""
+
+    def __init__(self, device, batches: Sequence["Batch"], on_device: bool = True):
+        self.device, self.on_device = device, on_device
+        pin = lambda n: torch.empty(n, dtype=torch.int32, pin_memory=True)  # noqa: E731
+        dev = lambda n: torch.empty(max(n, 1), dtype=torch.int32, device=device)  # noqa: E731
+        if on_device:
+            n = [2 * len(b.prompts) + 1 + b.tokens for b in batches]  # offsets | ids | last-token rows
+            self.host = [[pin(k) for k in n] for _ in range(2)]
+            # per slot and chunk: packed input, then token_node, node_token, node_depth, node_prompt
+            self.dev_in = [[dev(k) for k in n] for _ in range(2)]
+            self.dev_out = [[[dev(b.tokens) for _ in range(4)] for b in batches] for _ in range(2)]
+            self.count_dev = [dev(len(batches)) for _ in range(2)]
+            self.count_host = [pin(len(batches)) for _ in range(2)]
+            self.ws = [ops.TrieWorkspace(len(b.prompts), device) for b in batches]
+            _, high = torch.cuda.Stream.priority_range()
+            self.stream = torch.cuda.Stream(device, priority=high)
+        else:
+            n = [2 * b.rows + b.tokens + len(b.prompts) for b in batches]
+            self.host = [[pin(k) for k in n] for _ in range(2)]
+        self.done = [[None] * len(batches) for _ in range(2)]  # the copy that last read host[slot][c]
+        self.used = [None, None]                               # the step that last read slot's outputs
         self.slot = 0
+
+    def mark_used(self) -> None:
+        """Records, on the current stream, that the step just enqueued is the
+        last reader of this slot's device buffers."""
+        ev = torch.cuda.Event()
+        ev.record()
+        self.used[self.slot] = ev
 
     def upload(self, c: int, prompts: Sequence[np.ndarray]) -> "Batch":
         if c == 0:
             self.slot ^= 1
+        return self._upload_device(c, prompts) if self.on_device else self._upload_host(c, prompts)
+
+    def _fill(self, c: int, parts) -> torch.Tensor:
+        n = sum(int(a.size) for a in parts)
+        if self.done[self.slot][c] is not None:
+            self.done[self.slot][c].synchronize()
+        buf = self.host[self.slot][c]
+        if buf.numel() < n:
+            raise ValueError("HostStage: a batch larger than the one it was sized for")
+        view, k = buf.numpy(), 0
+        for a in parts:
+            view[k:k + a.size] = a.view(np.int32)
+            k += a.size
+        return buf[:n]
+
+    def _upload_host(self, c: int, prompts) -> "Batch":
         trie = ops.prefix_trie(prompts)
         lens = np.array([len(p) for p in prompts])
         last = trie.token_node[np.cumsum(lens) - 1]
         parts = [trie.node_token, trie.node_depth, trie.token_node, last]
-        n = sum(int(a.size) for a in parts)
-        if self.done[self.slot][c] is not None:
-            self.done[self.slot][c].synchronize()  # the copy that last read this buffer
-        buf = self.host[self.slot][c]
-        if buf is None or buf.numel() < n:
-            buf = self.host[self.slot][c] = torch.empty(n, dtype=torch.int32, pin_memory=True)
-        view = buf.numpy()
-        k = 0
-        for a in parts:
-            view[k:k + a.size] = a.view(np.int32)
-            k += a.size
-        dev = torch.empty(n, dtype=torch.int32, device=self.device)
-        dev.copy_(buf[:n], non_blocking=True)
+        src = self._fill(c, parts)
+        dev = torch.empty(src.numel(), dtype=torch.int32, device=self.device)
+        dev.copy_(src, non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
         self.done[self.slot][c] = ev
@@ -296,7 +328,42 @@ class HostStage:
         for a in parts:
             out.append(dev[k:k + a.size])
             k += a.size
-        return Batch(list(prompts), trie, out[0], out[1], out[2], out[3], int(lens.max()))
+        return Batch(list(prompts), trie, out[0], out[1], out[2], out[3], int(lens.max()), trie.nodes,
+                     int(lens.sum()))
+
+    def _upload_device(self, c: int, prompts) -> "Batch":
+        s, slot = self.stream, self.slot
+        lens = np.array([len(p) for p in prompts], dtype=np.int64)
+        offs = np.zeros(len(prompts) + 1, np.int32)
+        offs[1:] = np.cumsum(lens)
+        total = int(offs[-1])
+        ids = np.concatenate([np.asarray(p, dtype=np.int32) for p in prompts])
+        ends = offs[1:] - 1
+        src = self._fill(c, [offs, ids, ends])
+        dev_in = self.dev_in[slot][c]
+        tn, nt, nd, npr = self.dev_out[slot][c]
+        if self.used[slot] is not None:
+            s.wait_event(self.used[slot])  # the step two back has finished with these buffers
+        with torch.cuda.stream(s):
+            dev_in[:src.numel()].copy_(src, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(s)
+            self.done[slot][c] = done
+            offsets, ids_d = dev_in[:offs.size], dev_in[offs.size:offs.size + total]
+            ends_d = dev_in[offs.size + total:offs.size + total + ends.size]
+            ws = self.ws[c]
+            ops._check(ops._lib.lib().b2_prefix_trie_device(
+                ids_d.data_ptr(), offsets.data_ptr(), len(prompts), total, VOCAB, 4096, tn.data_ptr(),
+                nt.data_ptr(), nd.data_ptr(), npr.data_ptr(), self.count_dev[slot][c:c + 1].data_ptr(),
+                ws.buf.data_ptr(), ws.bytes, s.cuda_stream), "prefix_trie_device")
+            last = torch.index_select(tn, 0, ends_d)
+            self.count_host[slot][c:c + 1].copy_(self.count_dev[slot][c:c + 1], non_blocking=True)
+            built = torch.cuda.Event()
+            built.record(s)
+        built.synchronize()  # the node count sizes this chunk's launches
+        nodes = int(self.count_host[slot][c])
+        torch.cuda.current_stream(self.device).wait_event(built)
+        return Batch(list(prompts), None, nt[:nodes], nd[:nodes], tn[:total], last, int(lens.max()), nodes, total)
 
 
 class ShardedPrefill:
@@ -314,7 +381,7 @@ class ShardedPrefill:
 
     def __init__(self, prompts: Sequence[np.ndarray], plan: list, weights: Weights, device,
                  standins: Sequence[StandIns], layers: int, rank: int = 0, exact: bool = False, group=None,
-                 concurrent: bool = True):
+                 concurrent: bool = True, device_trie: bool = True):
         """`plan` is shard.chunk_plan(prompts, world, chunks): this rank runs
         plan[rank]; every rank's chunk c must have the same token count (the
         per-chunk gather moves equal-sized buffers)."""
@@ -340,7 +407,7 @@ class ShardedPrefill:
         self.recv = None
         if world > 1 and rank == 0:
             self.recv = [[torch.empty_like(t) for _ in range(world)] for t in self.send]
-        self._stage = HostStage(device, self.batches)
+        self._stage = HostStage(device, self.batches, on_device=device_trie)
         self._last_idx = None
         self.streams = None
         if concurrent and len(self.pipes) > 1:
@@ -380,18 +447,23 @@ class ShardedPrefill:
                 cur.wait_stream(s)
         for w in works:  # cur waits for the collective's stream
             w.wait()
+        self._stage.mark_used()
 
     def rebuild(self) -> int:
-        """The host part of an end-to-end step: rebuilds every chunk's trie
-        from host token ids and uploads its index arrays (one copy per chunk
-        from a reused pinned buffer, asynchronous on the current stream);
-        returns the H2D bytes."""
+        """The host part of an end-to-end step: every chunk's trie from host
+        token ids (HostStage: built on the device from the uploaded ids by
+        default, else on the host); returns the H2D bytes."""
         nbytes = 0
         for c, ps in enumerate(self.prompts):
             b = self._stage.upload(c, ps)
+            if b.rows != self.pipes[c].shape.rows:
+                raise ValueError("rebuild: the prompts' trie differs from the one the pipeline was sized for")
             self.pipes[c].batch = b
             self.batches[c] = b
-            nbytes += sum(int(t.numel()) * 4 for t in (b.node_token, b.node_depth, b.token_node, b.last_rows))
+            if self._stage.on_device:
+                nbytes += (2 * len(ps) + 1 + b.tokens) * 4
+            else:
+                nbytes += sum(int(t.numel()) * 4 for t in (b.node_token, b.node_depth, b.token_node, b.last_rows))
         return nbytes
 
     def last_token_rows(self, out: torch.Tensor) -> None:

@@ -107,7 +107,7 @@ def _grouped_prompts(seed=13):
     return out
 
 
-def _sharded(cuda, prompts, plan, concurrent, layers=2, pool=2):
+def _sharded(cuda, prompts, plan, concurrent, layers=2, pool=2, device_trie=True):
     import torch
 
     from aps2026_b200 import prefill
@@ -116,14 +116,17 @@ def _sharded(cuda, prompts, plan, concurrent, layers=2, pool=2):
     rows = prefill.ShardedPrefill.rows_needed(prompts, plan[0])
     gen = torch.Generator(device=cuda).manual_seed(21)  # same stand-ins for every runner
     sets = [prefill.StandIns.make(rows, cuda, gen) for _ in range(pool)]
-    return prefill.ShardedPrefill(prompts, plan, w, cuda, sets, layers, exact=True, concurrent=concurrent)
+    return prefill.ShardedPrefill(prompts, plan, w, cuda, sets, layers, exact=True, concurrent=concurrent,
+                                  device_trie=device_trie)
 
 
-def test_sharded_concurrent_chunks_match_serial_and_rebuild(cuda):
+@pytest.mark.parametrize("device_trie", [True, False])
+def test_sharded_concurrent_chunks_match_serial_and_rebuild(cuda, device_trie):
     """One rank, three chunks: chunks on concurrent prioritised streams give
     the same token rows as one stream, bit for bit; so does an end-to-end
-    step whose tries are rebuilt on the host and uploaded from the reused
-    pinned buffers (rebuilt twice, to cycle both buffers)."""
+    step whose tries are rebuilt from host token ids -- on the device, or on
+    the host and uploaded -- through the reused pinned buffers (rebuilt
+    twice, to cycle both buffer sets)."""
     import torch
 
     from aps2026_b200.shard import chunk_plan
@@ -136,7 +139,7 @@ def test_sharded_concurrent_chunks_match_serial_and_rebuild(cuda):
     conc = _sharded(cuda, prompts, plan, concurrent=True)
     assert conc.streams is not None
     conc.step()
-    e2e = _sharded(cuda, prompts, plan, concurrent=True)
+    e2e = _sharded(cuda, prompts, plan, concurrent=True, device_trie=device_trie)
     for _ in range(2):
         e2e.rebuild()
         for b, b0 in zip(e2e.batches, serial.batches):
