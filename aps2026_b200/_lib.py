@@ -45,6 +45,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_rope": (C.c_int, [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _sz, _vp]),
     "b2_causal_softmax": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _f32, _sz, _u32, _vp]),
     "b2_attention_tree": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _u32, _vp]),
+    "b2_attention_tree_compact": (C.c_int, [_vp] * 7 + [_sz, _vp] + [_sz] * 7 + [_u32, _vp]),
     "b2_moe_route_workspace_size": (C.c_int, [_sz, _sz, _vp]),
     "b2_moe_route": (C.c_int, [_vp, _sz, _sz, _f32, _f32] + [_vp] * 10 + [_sz, _vp]),
     "b2_moe_route_noalloc": (C.c_int, [_vp, _sz, _sz, _f32, _f32] + [_vp] * 9 + [_vp]),

@@ -42,10 +42,29 @@ struct AttnArgs {
     const float* v;
     float* out;
     const std::uint32_t* row_pos;
-    const std::uint32_t* anc;
+    const std::uint32_t* anc;          // dense chains [rows][anc_stride], or null: compact chains
     std::size_t anc_stride, rows, q_heads, kv_heads, window, max_window;
     float scale;
+    // compact chains: node n's keys 0..pos are token_node[prompt_off[p] ..], p = node_prompt[n]
+    const std::uint32_t* node_prompt;
+    const std::uint32_t* prompt_off;   // [prompts + 1]
+    const std::uint32_t* token_node;   // [total]
+    std::size_t prompts, total;
 };
+
+// First key of the ancestor chain of row n at position pos (its keys are
+// [0, pos]), or null when the chain is not available: pos outside the dense
+// table's stride (or the longest prompt), or a compact witness prompt that
+// does not reach depth pos.
+__device__ __forceinline__ const std::uint32_t* chain_of(const AttnArgs& a, std::size_t n, std::size_t pos) {
+    if (pos >= a.anc_stride) return nullptr;
+    if (a.anc) return a.anc + n * a.anc_stride;
+    const std::uint32_t p = a.node_prompt[n];
+    if (p >= a.prompts) return nullptr;
+    const std::uint32_t o0 = a.prompt_off[p], o1 = a.prompt_off[p + 1];
+    if (o0 > o1 || o1 > a.total || pos >= o1 - o0) return nullptr;
+    return a.token_node + o0;
+}
 
 // Division by a row denominator d >= 1 with one reciprocal per row, as in
 // softmax.cu (Markstein's correction gives the correctly rounded quotient).
@@ -76,17 +95,18 @@ attention_tree_kernel(AttnArgs a) {
     const std::size_t row = task / a.kv_heads, kh = task % a.kv_heads;
     const unsigned tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const std::size_t pos = a.row_pos[row];
-    if (tid == 0) bad_s = pos >= a.anc_stride;
+    const std::uint32_t* row_chain = chain_of(a, row, pos);
+    if (tid == 0) bad_s = row_chain == nullptr;
     __syncthreads();
     float* out_row = a.out + (row * a.q_heads + kh * kGroup) * HD;
-    if (bad_s) {  // position outside the ancestor table: report, output zeros
+    if (bad_s) {  // no ancestor chain for this position: report, output zeros
         if (tid == 0) flag_check(B2_CHECK_ATTENTION);
         for (int i = tid; i < kGroup * HD; i += kAttnThreads) out_row[i] = 0.0f;
         return;
     }
     const std::size_t begin = pos + 1 > a.window ? pos + 1 - a.window : 0;
     const int W = static_cast<int>(pos - begin + 1);
-    const std::uint32_t* anc_row = a.anc + row * a.anc_stride + begin;
+    const std::uint32_t* anc_row = row_chain + begin;
     for (int i = tid; i < W; i += kAttnThreads) {
         std::uint32_t c = anc_row[i];
         if (c >= a.rows) {
@@ -310,7 +330,7 @@ struct BlockAttention {
         const std::size_t p0 = a.row_pos[first], P = a.row_pos[last];
         const std::size_t begin = p0 + 1 > a.window ? p0 + 1 - a.window : 0;
         const int wg = static_cast<int>(P - begin + 1);
-        const std::uint32_t* anc_last = a.anc + last * a.anc_stride + begin;
+        const std::uint32_t* anc_last = chain_of(a, last, P) + begin;  // checked by the caller
         for (int i = tid; i < wg; i += kBlkThreads) {
             std::uint32_t c = anc_last[i];
             if (c >= a.rows) {
@@ -320,7 +340,7 @@ struct BlockAttention {
             chain[i] = c;
         }
         __syncthreads();  // chain complete (fetch reads other threads' entries)
-        if (verify && g > 1) {
+        if (verify && g > 1 && a.anc) {  // compact chains of one prompt agree by construction
             int differs = 0;
             for (int r = 0; r + 1 < g; ++r) {
                 const std::size_t pr = p0 + r;
@@ -543,11 +563,14 @@ attention_tree_block(AttnArgs a, std::size_t wcap) {
         seg_s[0] = 0;
         std::size_t prev = 0;
         for (int r = 0; r < nrows; ++r) {
-            const std::size_t pos = a.row_pos[n0 + r];
-            bad_s[r] = pos >= a.anc_stride;
+            const std::size_t n = n0 + r, pos = a.row_pos[n];
+            bad_s[r] = chain_of(a, n, pos) == nullptr;
             if (r > 0) {
+                // dense: the parent entry of row n is n - 1; compact: the same
+                // witness prompt one position further
                 const bool link = !bad_s[r] && !bad_s[r - 1] && pos == prev + 1 &&
-                                  a.anc[(n0 + r) * a.anc_stride + pos - 1] == n0 + r - 1;
+                                  (a.anc ? a.anc[n * a.anc_stride + pos - 1] == n - 1
+                                         : a.node_prompt[n] == a.node_prompt[n - 1]);
                 if (!link) seg_s[++nseg] = r;
             }
             prev = pos;
@@ -589,13 +612,15 @@ int launch_attention(const AttnArgs& a, cudaStream_t s) {
 
 B2_DEFINE_CHECK_TAKER(attention)
 
-extern "C" int b2_attention_tree(const float* q, const float* k, const float* v, float* out,
-                                 const uint32_t* row_pos, const uint32_t* anc, size_t anc_stride, size_t rows,
-                                 size_t q_heads, size_t kv_heads, size_t head_dim, size_t window, uint32_t flags,
-                                 b2_stream_t stream) {
-    using namespace b2;
-    if (rows == 0) return B2_OK;
-    if (!q || !k || !v || !out || !row_pos || !anc) return invalid("b2_attention_tree: null pointer");
+namespace b2 {
+namespace {
+
+// Shared by both entry points once the chain source is set in `a`.
+int attention_launch(AttnArgs& a, std::size_t head_dim, std::uint32_t flags, b2_stream_t stream) {
+    const std::size_t rows = a.rows, kv_heads = a.kv_heads, q_heads = a.q_heads, window = a.window;
+    const std::size_t anc_stride = a.anc_stride;
+    const float *q = a.q, *k = a.k, *v = a.v;
+    float* out = a.out;
     if (kv_heads == 0 || q_heads != kGroup * kv_heads)
         return invalid("attention_tree_gpu expects GQA-4");
     if (head_dim != 128 && head_dim != 64)
@@ -603,8 +628,8 @@ extern "C" int b2_attention_tree(const float* q, const float* k, const float* v,
     if (window == 0 || anc_stride == 0) return invalid("b2_attention_tree: window / anc_stride is 0");
     if (rows * kv_heads > 0x7FFFFFFFu) return invalid("b2_attention_tree: too many rows");
     if (!aligned16(k) || !aligned16(v)) return invalid("b2_attention_tree: k / v not 16-byte aligned");
-    AttnArgs a{q, k, v, out, row_pos, anc, anc_stride, rows, q_heads, kv_heads, window,
-               window < anc_stride ? window : anc_stride, 1.0f / sqrtf(static_cast<float>(head_dim))};
+    a.max_window = window < anc_stride ? window : anc_stride;
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
     const bool exact = (flags & B2_FLAG_EXACT_ORDER) != 0;
     cudaStream_t s = as_stream(stream);
     const std::size_t wcap = (a.max_window + kBlkRows - 1 + 3) & ~std::size_t(3);
@@ -623,4 +648,39 @@ extern "C" int b2_attention_tree(const float* q, const float* k, const float* v,
     else rc = exact ? launch_attention<64, true>(a, s) : launch_attention<64, false>(a, s);
     if (rc) return rc;
     return launch_result("b2_attention_tree");
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" int b2_attention_tree(const float* q, const float* k, const float* v, float* out,
+                                 const uint32_t* row_pos, const uint32_t* anc, size_t anc_stride, size_t rows,
+                                 size_t q_heads, size_t kv_heads, size_t head_dim, size_t window, uint32_t flags,
+                                 b2_stream_t stream) {
+    using namespace b2;
+    if (rows == 0) return B2_OK;
+    if (!q || !k || !v || !out || !row_pos || !anc) return invalid("b2_attention_tree: null pointer");
+    AttnArgs a{};
+    a.q = q; a.k = k; a.v = v; a.out = out; a.row_pos = row_pos; a.anc = anc; a.anc_stride = anc_stride;
+    a.rows = rows; a.q_heads = q_heads; a.kv_heads = kv_heads; a.window = window;
+    return attention_launch(a, head_dim, flags, stream);
+}
+
+extern "C" int b2_attention_tree_compact(const float* q, const float* k, const float* v, float* out,
+                                         const uint32_t* row_pos, const uint32_t* node_prompt,
+                                         const uint32_t* prompt_offsets, size_t prompts, const uint32_t* token_node,
+                                         size_t total_tokens, size_t max_len, size_t rows, size_t q_heads,
+                                         size_t kv_heads, size_t head_dim, size_t window, uint32_t flags,
+                                         b2_stream_t stream) {
+    using namespace b2;
+    if (rows == 0) return B2_OK;
+    if (!q || !k || !v || !out || !row_pos || !node_prompt || !prompt_offsets || !token_node)
+        return invalid("b2_attention_tree_compact: null pointer");
+    if (prompts == 0 || total_tokens == 0) return invalid("b2_attention_tree_compact: empty batch");
+    AttnArgs a{};
+    a.q = q; a.k = k; a.v = v; a.out = out; a.row_pos = row_pos; a.anc = nullptr; a.anc_stride = max_len;
+    a.rows = rows; a.q_heads = q_heads; a.kv_heads = kv_heads; a.window = window;
+    a.node_prompt = node_prompt; a.prompt_off = prompt_offsets; a.token_node = token_node;
+    a.prompts = prompts; a.total = total_tokens;
+    return attention_launch(a, head_dim, flags, stream);
 }

@@ -230,6 +230,25 @@ def attention_tree_gpu(q, k, v, out, row_pos, anc, anc_stride: int, rows: int, q
            "attention_tree_gpu")
 
 
+def attention_tree_compact_gpu(q, k, v, out, row_pos, node_prompt, prompt_offsets, token_node, max_len: int,
+                               rows: int, q_heads: int, kv_heads: int, head_dim: int,
+                               window: int = SLIDING_WINDOW, exact: bool = False) -> None:
+    """attention_tree_gpu with compact ancestor chains (the node witnesses of
+    prefix_trie_device): row r's chain is token_node[prompt_offsets[p]:][:pos + 1],
+    p = node_prompt[r]."""
+    if q_heads != 4 * kv_heads:
+        raise InvalidArgument("attention_tree_gpu expects GQA-4")
+    prompts = prompt_offsets.numel() - 1
+    if (q.numel() != rows * q_heads * head_dim or out.numel() != q.numel()
+            or k.numel() != rows * kv_heads * head_dim or v.numel() != k.numel()
+            or row_pos.numel() != rows or node_prompt.numel() != rows or prompts < 1):
+        raise InvalidArgument("attention shape")
+    _check(_lib.lib().b2_attention_tree_compact(
+        _f32(q), _f32(k), _f32(v), _f32(out), _u32(row_pos), _u32(node_prompt), _u32(prompt_offsets), prompts,
+        _u32(token_node), token_node.numel(), max_len, rows, q_heads, kv_heads, head_dim, window, _flags(exact),
+        _stream()), "attention_tree_compact_gpu")
+
+
 # ---- MoE ----------------------------------------------------------------------------------
 
 

@@ -198,6 +198,25 @@ int b2_attention_tree(const float* q, const float* k, const float* v,
                       size_t q_heads, size_t kv_heads, size_t head_dim,
                       size_t window, uint32_t flags, b2_stream_t stream);
 
+/*
+ * b2_attention_tree with the compact ancestor form of b2_prefix_trie_device
+ * instead of the dense [rows, anc_stride] table (1 GB at 64 x 2048 tokens;
+ * no reference counterpart): row r's chain is
+ * token_node[prompt_offsets[p] .. + pos], p = node_prompt[r], so only the
+ * packed token_node array [total_tokens] is read. max_len bounds the
+ * positions (the longest prompt). Same kernels, arithmetic and results as
+ * b2_attention_tree on the equivalent dense table; a row whose witness
+ * prompt does not reach its position is reported like a bad position.
+ */
+int b2_attention_tree_compact(const float* q, const float* k, const float* v,
+                              float* out, const uint32_t* row_pos,
+                              const uint32_t* node_prompt,
+                              const uint32_t* prompt_offsets, size_t prompts,
+                              const uint32_t* token_node, size_t total_tokens,
+                              size_t max_len, size_t rows, size_t q_heads,
+                              size_t kv_heads, size_t head_dim, size_t window,
+                              uint32_t flags, b2_stream_t stream);
+
 /* ---- MoE routing (bit-exact) ---------------------------------------------- */
 
 /* Bytes of caller workspace b2_moe_route needs for T tokens, E experts. */

@@ -113,3 +113,45 @@ def test_attention_tree_inconsistent_ancestors_fall_back_per_row(cuda):
     torch.cuda.synchronize()
     oracle.assert_bitexact(to_host(out), want, "attention, inconsistent ancestors")
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("hd", [128, 64])
+def test_attention_tree_compact_chains_match_dense(cuda, hd):
+    """The compact ancestor form (device trie witnesses + token_node) gives
+    the same outputs as the dense table, bit for bit, on a batch with shared
+    prefixes; a witness that does not reach a row's depth is reported."""
+    import torch
+
+    from aps2026_b200 import ops
+
+    g = rng(54)
+    base = g.integers(0, 500, 40)
+    prompts = [np.concatenate([base[:int(g.integers(0, 41))], g.integers(0, 500, int(g.integers(1, 200)))])
+               .astype(np.int32) for _ in range(7)]
+    ids = torch.from_numpy(np.concatenate(prompts)).to(cuda)
+    offs = np.zeros(len(prompts) + 1, np.int32)
+    offs[1:] = np.cumsum([len(p) for p in prompts])
+    offs_d = torch.from_numpy(offs).to(cuda)
+    dt = ops.prefix_trie_device(ids, offs_d, vocab=500)
+    t = oracle.prefix_trie(prompts, vocab=500)
+    R, stride = t["nodes"], t["node_anc"].shape[1]
+    assert dt.nodes == R
+    q, k, v = normal(g, (R, 16 * hd)), normal(g, (R, 4 * hd)), normal(g, (R, 4 * hd))
+    qd, kd, vd = to_dev(q, cuda), to_dev(k, cuda), to_dev(v, cuda)
+    pos = to_dev(t["node_depth"], cuda)
+    dense = torch.empty((R, 16 * hd), device=cuda)
+    ops.attention_tree_gpu(qd, kd, vd, dense, pos, to_dev(np.ascontiguousarray(t["node_anc"]), cuda), stride, R, 16,
+                           4, hd, 2047, exact=True)
+    compact = torch.full_like(dense, float("nan"))
+    ops.attention_tree_compact_gpu(qd, kd, vd, compact, pos, dt.node_prompt, offs_d, dt.token_node, stride, R, 16, 4,
+                                   hd, 2047, exact=True)
+    torch.cuda.synchronize()
+    assert torch.equal(compact, dense)
+    assert ops.device_status() == 0
+    bad = dt.node_prompt.clone()
+    deep = int(np.argmax(t["node_depth"]))
+    short = int(np.argmin([len(p) for p in prompts]))
+    bad[deep] = short  # that prompt is shorter than the node's depth
+    ops.attention_tree_compact_gpu(qd, kd, vd, compact, pos, bad, offs_d, dt.token_node, stride, R, 16, 4, hd, 2047)
+    assert ops.device_status() & 8
+    assert torch.equal(compact[deep], torch.zeros_like(compact[deep]))
