@@ -52,7 +52,9 @@ static __device__ __noinline__ float exp_ref_slow(float x) {
 // ties are among the near-midpoint cases sent to the slow path).
 __device__ __forceinline__ float exp_ref_fast(float x, const double* tab, bool* slow) {
     const bool out_of_range = !(fabsf(x) <= 80.0f);     // also NaN
-    const double xd = static_cast<double>(out_of_range ? 0.0f : x);
+    // (out of range, the steps below compute garbage -- j stays a valid table
+    // index -- and the result is discarded)
+    const double xd = static_cast<double>(x);
     const double shifter = 6755399441055744.0;          // 1.5 * 2^52
     const double tn = fma(xd, 92.332482616893656877, shifter);  // x * 64 / ln2, rounded to an integer
     const int n = __double2loint(tn);                   // that integer (|n| < 2^13)
@@ -68,7 +70,7 @@ __device__ __forceinline__ float exp_ref_fast(float x, const double* tab, bool* 
     const double y = fma(t, p, t);                      // 2^(j/64) e^r, in [0.99, 2)
     const int lo = __double2loint(y);
     const int low29 = lo & 0x1FFFFFFF;
-    *slow = out_of_range | (abs(low29 - 0x10000000) < 2048);
+    *slow = out_of_range | (static_cast<unsigned>(low29 - (0x10000000 - 2047)) < 4095u);  // |low29 - 2^28| < 2048
     const int hi = __double2hiint(y) + static_cast<int>(static_cast<unsigned>(m) << 20);  // y * 2^m
     return __double2float_rn(__hiloint2double(hi, lo));
 }
