@@ -287,19 +287,20 @@ struct BlockAttention {
 
     // Issues the copies of the 32 chain rows of tile t into buffer t & 1:
     // keys transposed to [key][j][i] (d = 4i + j), one 4-byte copy per
-    // element, consecutive threads on consecutive d of one key (coalesced;
-    // 16 consecutive d per thread measured 30% slower); values as [key][d],
-    // one 16-byte copy per 4 elements. Rows past wg are skipped.
+    // element; values as [key][d], one 16-byte copy per 4 elements. Rows past
+    // wg are skipped. For the keys, 8 threads share a key row: thread x
+    // copies d = x, x + 8, ..., so a warp's copy covers four whole 32-byte
+    // sectors, each thread looks up its chain entry once, and its elements
+    // all fall in one d-mod-4 slice (j = x mod 4), two positions apart.
     __device__ __forceinline__ void issue_keys(int t, int wg) const {
-        const std::size_t row = a.kv_heads * 128;
-        float* buf = tile + (t & 1) * kTileFloats;
+        static_assert(kBlkKeys * 8 == kBlkThreads, "8 threads per staged key row");
+        const int ks = static_cast<int>(tid >> 3), x = static_cast<int>(tid & 7);
+        const int w = t * kBlkKeys + ks;
+        if (w < wg) {
+            const float* src = a.k + static_cast<std::size_t>(chain[w]) * (a.kv_heads * 128) + kh * 128 + x;
+            float* dst = tile + (t & 1) * kTileFloats + ks * kKeyPitch + (x & 3) * kJStride + (x >> 2);
 #pragma unroll
-        for (int u = 0; u < kBlkKeys * 128 / kBlkThreads; ++u) {
-            const int i = static_cast<int>(tid) + u * kBlkThreads, ks = i >> 7, d = i & 127;
-            const int w = t * kBlkKeys + ks;
-            if (w < wg)
-                cp_async4(buf + ks * kKeyPitch + (d & 3) * kJStride + (d >> 2),
-                          a.k + static_cast<std::size_t>(chain[w]) * row + kh * 128 + d);
+            for (int u = 0; u < 16; ++u) cp_async4(dst + 2 * u, src + 8 * u);
         }
         cp_async_commit();
     }
