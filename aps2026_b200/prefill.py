@@ -7,8 +7,9 @@ The GEMM outputs of each layer (q/k projections, attention + o_proj, router
 logits, expert gate/up and W2 outputs) are supplied as seeded stand-in
 tensors of the config.h shapes (``StandIns``): the projections are outside
 this path. Everything on the path itself runs through the C ABI
-(``b2_prefill_layers`` for the layer loop, ``b2_prefix_trie_build`` for the
-trie, ``b2_gather_rows`` for the expansion back to token rows).
+(``b2_prefill_layers`` for the layer loop, ``b2_prefix_trie_build`` or, for
+end-to-end steps, ``b2_prefix_trie_device`` for the trie, ``b2_gather_rows``
+for the expansion back to token rows).
 """
 from __future__ import annotations
 
