@@ -44,7 +44,7 @@ struct SoftmaxArgs {
 // FMA-pipe operations instead of a full division per element; arguments
 // below 2^-96, whose residual could leave the normal range, divide directly.
 __device__ __forceinline__ float div_by_row(float e, float d, float y) {
-    if (e < 0x1p-96f) return e == 0.0f ? 0.0f : __fdiv_rn(e, d);
+    if (e < 0x1p-96f) return __fdiv_rn(e, d);  // (0 / NaN must stay NaN)
     const float q = __fmul_rn(e, y);
     const float r = __fmaf_rn(-d, q, e);
     return __fmaf_rn(r, y, q);

@@ -158,7 +158,7 @@ def test_rope_table_matches_oracle(ops):
 
 
 @pytest.mark.parametrize("heads,T,window", [(2, 2048, 2047), (1, 2048, 4096), (3, 64, 2047), (2, 256, 100),
-                                              (2, 37, 2047), (1, 8192, 2047)])
+                                              (2, 37, 2047), (1, 4096, 2047), (1, 8192, 2047)])
 @pytest.mark.parametrize("exact", [False, True])
 def test_causal_softmax(ops, cuda, heads, T, window, exact):
     import torch
@@ -180,6 +180,32 @@ def test_causal_softmax(ops, cuda, heads, T, window, exact):
         j = np.arange(T)[None, :]
         masked = (j > i) | (j < i + 1 - window)
         assert (got[:, masked] == 0).all()
+
+
+@pytest.mark.parametrize("T", [256, 2048])
+def test_causal_softmax_extreme_scores(ops, cuda, T):
+    """Wide scores: exponentials that underflow to exactly 0 (below -104) or
+    are tiny enough for the direct division, next to ordinary ones; and
+    +-inf scores, whose rows must match the reference's arithmetic."""
+    import torch
+
+    g = rng(41)
+    s = normal(g, (2, T, T), std=600.0)
+    s[1, 5, :3] = np.float32(-np.inf)
+    s[1, 7, 2] = np.float32(np.inf)
+    scale = np.float32(1.0 / math.sqrt(128.0))
+    want = oracle.causal_softmax(s, scale, 2047)
+    for exact in (True, False):
+        probs = torch.full((2, T, T), float("nan"), device=cuda)
+        ops.causal_softmax_gpu(to_dev(s, cuda), probs, float(scale), 2047, exact=exact)
+        _sync()
+        got = to_host(probs)
+        finite = np.isfinite(want)
+        assert (np.isnan(got) == np.isnan(want)).all()
+        if exact:
+            oracle.assert_bitexact(got[finite], want[finite], "softmax exact, wide scores")
+        else:
+            oracle.assert_close(got[finite], want[finite], what="softmax, wide scores")
 
 
 # ---- MoE routing ---------------------------------------------------------------------------
