@@ -257,8 +257,9 @@ class HostStage:
     Device mode (default): packs [offsets | ids] into a pinned buffer, copies
     it up asynchronously and builds the trie on the GPU
     (b2_prefix_trie_device) on a high-priority stream of its own, so the
-    build overlaps the previous step still running; only the node count
-    comes back (the host needs it to size the launches). Host mode: builds
+    build overlaps the previous step still running; only the node counts
+    come back (the host needs them to size the launches), read once per step
+    after every chunk's build is enqueued. Host mode: builds
     the trie on the host (b2_prefix_trie_build) and copies its index arrays
     up on the current stream.
 
@@ -296,10 +297,25 @@ class HostStage:
         ev.record()
         self.used[self.slot] = ev
 
-    def upload(self, c: int, prompts: Sequence[np.ndarray]) -> "Batch":
-        if c == 0:
-            self.slot ^= 1
-        return self._upload_device(c, prompts) if self.on_device else self._upload_host(c, prompts)
+    def upload_all(self, chunks: Sequence[Sequence[np.ndarray]]) -> "list[Batch]":
+        """One Batch per chunk of prompts (the chunks the stage was sized
+        for). Device mode launches every chunk's build before it reads the
+        node counts back, so the host waits once per step."""
+        self.slot ^= 1
+        if not self.on_device:
+            return [self._upload_host(c, ps) for c, ps in enumerate(chunks)]
+        pending = [self._launch_device(c, ps) for c, ps in enumerate(chunks)]
+        built = torch.cuda.Event()
+        built.record(self.stream)
+        built.synchronize()  # the node counts size the chunks' launches
+        torch.cuda.current_stream(self.device).wait_event(built)
+        out = []
+        for c, (prompts, lens, total, last) in enumerate(pending):
+            tn, nt, nd, _ = self.dev_out[self.slot][c]
+            nodes = int(self.count_host[self.slot][c])
+            out.append(Batch(list(prompts), None, nt[:nodes], nd[:nodes], tn[:total], last, int(lens.max()), nodes,
+                             total))
+        return out
 
     def _fill(self, c: int, parts) -> torch.Tensor:
         n = sum(int(a.size) for a in parts)
@@ -332,7 +348,7 @@ class HostStage:
         return Batch(list(prompts), trie, out[0], out[1], out[2], out[3], int(lens.max()), trie.nodes,
                      int(lens.sum()))
 
-    def _upload_device(self, c: int, prompts) -> "Batch":
+    def _launch_device(self, c: int, prompts):
         s, slot = self.stream, self.slot
         lens = np.array([len(p) for p in prompts], dtype=np.int64)
         offs = np.zeros(len(prompts) + 1, np.int32)
@@ -359,12 +375,7 @@ class HostStage:
                 ws.buf.data_ptr(), ws.bytes, s.cuda_stream), "prefix_trie_device")
             last = torch.index_select(tn, 0, ends_d)
             self.count_host[slot][c:c + 1].copy_(self.count_dev[slot][c:c + 1], non_blocking=True)
-            built = torch.cuda.Event()
-            built.record(s)
-        built.synchronize()  # the node count sizes this chunk's launches
-        nodes = int(self.count_host[slot][c])
-        torch.cuda.current_stream(self.device).wait_event(built)
-        return Batch(list(prompts), None, nt[:nodes], nd[:nodes], tn[:total], last, int(lens.max()), nodes, total)
+        return prompts, lens, total, last
 
 
 class ShardedPrefill:
@@ -455,8 +466,7 @@ class ShardedPrefill:
         token ids (HostStage: built on the device from the uploaded ids by
         default, else on the host); returns the H2D bytes."""
         nbytes = 0
-        for c, ps in enumerate(self.prompts):
-            b = self._stage.upload(c, ps)
+        for c, (ps, b) in enumerate(zip(self.prompts, self._stage.upload_all(self.prompts))):
             if b.rows != self.pipes[c].shape.rows:
                 raise ValueError("rebuild: the prompts' trie differs from the one the pipeline was sized for")
             self.pipes[c].batch = b
