@@ -54,6 +54,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_add": (C.c_int, [_vp, _vp, _sz, _vp]),
     "b2_prefix_trie_build": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _sz, _vp]),
     "b2_selfcheck_exp": (C.c_int, [_u32, _u32, _vp, _vp, _vp]),
+    "b2_selfcheck_wait": (C.c_int, [C.c_uint64]),
     # struct arguments (b2_prefill_shape / _layer / _work) are passed by address
     "b2_prefill_layers": (C.c_int, [_vp, _vp, _sz, _vp, _vp, _vp, _vp, _sz, _vp, _sz, _vp, _vp, _vp, _vp, _vp,
                                     _vp, _vp]),

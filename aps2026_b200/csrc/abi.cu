@@ -53,6 +53,7 @@ int take_check_rope(cudaStream_t, unsigned int*);
 int take_check_moe(cudaStream_t, unsigned int*);
 int take_check_attention(cudaStream_t, unsigned int*);
 int take_check_trie(cudaStream_t, unsigned int*);
+int take_check_selfcheck(cudaStream_t, unsigned int*);
 
 }  // namespace b2
 
@@ -73,6 +74,7 @@ int b2_device_status(uint32_t* status_out, b2_stream_t stream) {
     if ((rc = b2::take_check_moe(s, &acc)) != B2_OK) return rc;
     if ((rc = b2::take_check_attention(s, &acc)) != B2_OK) return rc;
     if ((rc = b2::take_check_trie(s, &acc)) != B2_OK) return rc;
+    if ((rc = b2::take_check_selfcheck(s, &acc)) != B2_OK) return rc;
     *status_out = acc;
     return B2_OK;
 }

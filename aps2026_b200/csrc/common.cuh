@@ -114,6 +114,62 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+// ---- bulk (TMA) copies completing on an mbarrier ------------------------------
+//
+// One thread arms the CTA's barrier with the byte count of a phase and issues
+// 1-D bulk copies global -> shared (no multicast); every thread then waits
+// for the phase with mbar_wait, which gives up after kMbarWaitNs of the
+// global timer (or kMbarMaxPolls polls) so no wait can hang the GPU.
+constexpr unsigned kMbarMaxPolls = 1u << 26;
+constexpr unsigned long long kMbarWaitNs = 1000000000ull;  // 1 s
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+    return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(std::uint64_t* bar, unsigned arrivals) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(arrivals) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(std::uint64_t* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+// Orders this thread's earlier generic accesses to shared memory before
+// later async-proxy (bulk copy) writes to it.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, std::uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+// Waits for the barrier phase of parity `parity`; false if it did not
+// complete within `limit_ns` (or kMbarMaxPolls polls).
+__device__ __forceinline__ bool mbar_wait(std::uint64_t* bar, unsigned parity,
+                                          unsigned long long limit_ns = kMbarWaitNs) {
+    const unsigned long long t0 = global_ns();
+    for (unsigned i = 0; i < kMbarMaxPolls; ++i) {
+        unsigned done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(done)
+            : "r"(smem_addr(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 255u) == 255u && global_ns() - t0 > limit_ns) return false;
+    }
+    return false;
+}
+
 // ---- in-kernel bounds checks -------------------------------------------------
 //
 // Every kernel that dereferences a caller-provided index checks it, skips

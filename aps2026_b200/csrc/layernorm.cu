@@ -251,6 +251,95 @@ ln_rows_smem(LnArgs a) {
     }
 }
 
+// Rows too long for registers, h % 4 == 0 and 16-byte aligned: each row's
+// inputs (x; x and the residual; or the two expert rows and the carry) are
+// staged in shared memory by 1-D bulk (TMA) copies issued by one thread and
+// completing on an mbarrier, then reduced and written like ln_rows_smem.
+// Copies of an expert row outside expert_out are not issued (the row reads
+// as zeros, as in the register path). A wait that does not complete stops the
+// CTA and reports B2_CHECK_WAIT.
+template <int MODE, bool EXACT>
+__global__ void __launch_bounds__(256)
+ln_rows_bulk(LnArgs a) {
+    pdl_begin();
+    constexpr int THREADS = 256, WARPS = 8;
+    __shared__ float red[2][WARPS];
+    __shared__ float stats[2];
+    __shared__ __align__(8) std::uint64_t bar;
+    extern __shared__ __align__(128) float in[];  // NIN rows of h floats; in[0..h) becomes the sum
+    const std::size_t h = a.h;
+    const unsigned bytes = static_cast<unsigned>(h * sizeof(float));
+    const float hf = static_cast<float>(h);
+    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    __syncthreads();
+    unsigned parity = 0;
+    for (std::size_t r = blockIdx.x; r < a.rows; r += gridDim.x, parity ^= 1u) {
+        CombineRows cr{0, 0};
+        if (MODE == kCombineAddLN) cr = combine_rows(a.routes, a.route_positions, r, a.expert_rows);
+        const bool lo_ok = MODE == kCombineAddLN && cr.lo < a.expert_rows;
+        const bool hi_ok = MODE == kCombineAddLN && cr.hi < a.expert_rows;
+        if (threadIdx.x == 0) {
+            fence_proxy_async_smem();  // the previous row's shared accesses come first
+            if (MODE == kLN) {
+                mbar_expect_tx(&bar, bytes);
+                bulk_g2s(in, a.x + r * h, bytes, &bar);
+            } else if (MODE == kAddLN) {
+                mbar_expect_tx(&bar, 2 * bytes);
+                bulk_g2s(in, a.x + r * h, bytes, &bar);
+                bulk_g2s(in + h, a.res + r * h, bytes, &bar);
+            } else {
+                mbar_expect_tx(&bar, (1u + lo_ok + hi_ok) * bytes);
+                bulk_g2s(in, a.res + r * h, bytes, &bar);
+                if (lo_ok) bulk_g2s(in + h, a.expert_out + cr.lo * h, bytes, &bar);
+                if (hi_ok) bulk_g2s(in + 2 * h, a.expert_out + cr.hi * h, bytes, &bar);
+            }
+        }
+        if (__syncthreads_or(!mbar_wait(&bar, parity))) {  // a copy never landed: stop, report
+            if (threadIdx.x == 0) {
+                flag_check(B2_CHECK_WAIT);
+                mbar_wait(&bar, parity);  // one more bounded wait for the copies in flight
+            }
+            return;
+        }
+        float4* s4 = reinterpret_cast<float4*>(in);
+        const std::size_t h4 = h / 4;
+        if (MODE != kLN) {
+            for (std::size_t j = threadIdx.x; j < h4; j += THREADS) {
+                float4 v;
+                if (MODE == kAddLN) {
+                    v = add4(s4[j], s4[h4 + j]);
+                } else {
+                    const float4 lo = lo_ok ? s4[h4 + j] : zero4(), hi = hi_ok ? s4[2 * h4 + j] : zero4();
+                    v = add4(combine4(lo, hi), s4[j]);
+                }
+                s4[j] = v;
+                st_plain(reinterpret_cast<float4*>(a.x_out) + r * h4 + j, v);
+            }
+            __syncthreads();
+        }
+        float mean, inv;
+        if (EXACT) {
+            if (threadIdx.x == 0) serial_moments(in, h, a.eps, &stats[0], &stats[1]);
+            __syncthreads();
+            mean = stats[0];
+            inv = stats[1];
+        } else {
+            float part = 0.0f;
+            for (std::size_t j = threadIdx.x; j < h4; j += THREADS) part = __fadd_rn(part, sum4(s4[j]));
+            mean = __fdiv_rn(block_sum<WARPS>(part, red[0]), hf);
+            float part2 = 0.0f;
+            for (std::size_t j = threadIdx.x; j < h4; j += THREADS) part2 = __fadd_rn(part2, sqdev4(s4[j], mean));
+            inv = inv_std(block_sum<WARPS>(part2, red[1]), hf, a.eps);
+        }
+        const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+        const float4* b4 = reinterpret_cast<const float4*>(a.beta);
+        for (std::size_t j = threadIdx.x; j < h4; j += THREADS)
+            st_plain(reinterpret_cast<float4*>(a.y) + r * h4 + j,
+                     ln_out4(s4[j], mean, inv, __ldg(g4 + j), __ldg(b4 + j)));
+        __syncthreads();  // in[] is refilled for the next row
+    }
+}
+
 constexpr std::size_t kMaxSmemRow = 220 * 1024;  // + static reduction slots <= 227 KB
 
 template <int MODE, int THREADS, int V, bool EXACT>
@@ -261,6 +350,18 @@ int launch_reg(const LnArgs& a, cudaStream_t s) {
         return launch_result("layer norm: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), THREADS, smem, a.rows);
     launch_pdl(kernel, grid, THREADS, smem, s, a);
+    return B2_OK;
+}
+
+template <int MODE, bool EXACT>
+int launch_bulk(const LnArgs& a, cudaStream_t s) {
+    constexpr int NIN = MODE == kLN ? 1 : (MODE == kAddLN ? 2 : 3);
+    const std::size_t smem = NIN * a.h * sizeof(float);
+    auto kernel = ln_rows_bulk<MODE, EXACT>;
+    if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
+        return launch_result("layer norm: shared memory attribute");
+    const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), 256, smem, a.rows);
+    launch_pdl(kernel, grid, 256, smem, s, a);
     return B2_OK;
 }
 
@@ -276,7 +377,8 @@ int launch_smem(const LnArgs& a, cudaStream_t s) {
 }
 
 // Picks the register-resident variant whose THREADS * V covers h / 4, else
-// the shared-memory one.
+// bulk-copy staging (aligned rows, h % 4 == 0), else the scalar
+// shared-memory one.
 template <int MODE>
 int dispatch(const LnArgs& a, bool exact, bool vec_ok, cudaStream_t s, const char* what) {
     if (a.h * sizeof(float) > kMaxSmemRow && exact)
@@ -293,6 +395,8 @@ int dispatch(const LnArgs& a, bool exact, bool vec_ok, cudaStream_t s, const cha
         else if (h4 <= 256) rc = launch_reg<MODE, 128, 2, true>(a, s);
         else if (h4 <= 512) rc = launch_reg<MODE, 128, 4, true>(a, s);
         else rc = launch_reg<MODE, 128, 8, true>(a, s);
+    } else if (vec_ok && (MODE == kLN ? 1 : MODE == kAddLN ? 2 : 3) * a.h * sizeof(float) <= kMaxSmemRow) {
+        rc = exact ? launch_bulk<MODE, true>(a, s) : launch_bulk<MODE, false>(a, s);
     } else {
         if (a.h * sizeof(float) > kMaxSmemRow)
             return set_error(B2_ERR_UNSUPPORTED, std::string(what) + ": h too large");

@@ -33,8 +33,32 @@ exp_selfcheck(unsigned lo, unsigned hi, Counters* out) {
     atomicAdd(&out->slow, slow);
 }
 
+// A barrier armed for 16 bytes that no copy delivers: every wait on it must
+// give up within `limit_ns` and report B2_CHECK_WAIT (the bounded-wait path
+// of the bulk-copy kernels, exercised without any copy in flight).
+__global__ void __launch_bounds__(32)
+wait_selfcheck(unsigned long long limit_ns) {
+    __shared__ __align__(8) std::uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_expect_tx(&bar, 16);
+    }
+    __syncwarp();
+    const bool ok = mbar_wait(&bar, 0, limit_ns);
+    if (!ok && threadIdx.x == 0) flag_check(B2_CHECK_WAIT);
+}
+
 }  // namespace
 }  // namespace b2
+
+B2_DEFINE_CHECK_TAKER(selfcheck)
+
+extern "C" int b2_selfcheck_wait(uint64_t limit_ns) {
+    using namespace b2;
+    if (limit_ns == 0 || limit_ns > 10000000000ull) return invalid("b2_selfcheck_wait: limit_ns out of (0, 10 s]");
+    wait_selfcheck<<<1, 32>>>(limit_ns);
+    return launch_result("b2_selfcheck_wait");
+}
 
 extern "C" int b2_selfcheck_exp(uint32_t lo_bits, uint32_t hi_bits, uint64_t* checked, uint64_t* mismatches,
                                 uint64_t* slow_path) {

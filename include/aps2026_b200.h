@@ -74,6 +74,7 @@ const char* b2_last_error(void);
 #define B2_CHECK_COMBINE 4u
 #define B2_CHECK_ATTENTION 8u
 #define B2_CHECK_TRIE 16u
+#define B2_CHECK_WAIT 32u    /* a bounded wait for a bulk copy gave up; the CTA stopped */
 int b2_device_status(uint32_t* status_out, b2_stream_t stream);
 
 /* ---- embedding / row gather ---------------------------------------------- */
@@ -371,6 +372,15 @@ int b2_prefix_trie_device(const int32_t* ids, const uint32_t* offsets,
  */
 int b2_selfcheck_exp(uint32_t lo_bits, uint32_t hi_bits, uint64_t* checked,
                      uint64_t* mismatches, uint64_t* slow_path);
+
+/*
+ * Diagnostic, no reference counterpart: launches one warp that waits on a
+ * shared-memory barrier nothing completes, with the bounded wait the bulk-copy
+ * kernels use (limit_ns of the global timer, at most 10 s). The wait gives
+ * up, the kernel returns, and b2_device_status then reports B2_CHECK_WAIT;
+ * the context stays usable. Tests the failure path without any fault.
+ */
+int b2_selfcheck_wait(uint64_t limit_ns);
 
 /* ---- non-GEMM layer pipeline ------------------------------------------------ */
 

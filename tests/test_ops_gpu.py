@@ -63,7 +63,10 @@ def test_gather_rows_empty_and_bad_index(ops, cuda):
 
 # ---- LayerNorm ----------------------------------------------------------------------
 
-LN_SHAPES = [(512, 4096), (7, 4096), (3, 100), (5, 4100), (2, 12288), (1, 8192), (4, 2048)]
+# register rows (h <= 8192 tree order, <= 4096 exact order), bulk-copy staged
+# rows (aligned, h % 4 == 0, longer), scalar staged rows (h % 4 != 0)
+LN_SHAPES = [(512, 4096), (7, 4096), (3, 100), (5, 4100), (2, 12288), (1, 8192), (4, 2048), (3, 16384),
+             (2, 37)]
 
 
 @pytest.mark.parametrize("rows,h", LN_SHAPES)
@@ -302,7 +305,7 @@ def test_moe_combine_bitexact(ops, cuda, T, h):
     oracle.assert_bitexact(to_host(out), oracle.moe_combine(eo, r["routes"], r["route_positions"], T), "combine")
 
 
-@pytest.mark.parametrize("T,h", [(4096, 4096), (5, 100)])
+@pytest.mark.parametrize("T,h", [(4096, 4096), (5, 100), (3, 12288), (6, 8192)])
 @pytest.mark.parametrize("exact", [False, True])
 def test_moe_combine_add_layer_norm(ops, cuda, T, h, exact):
     import torch
@@ -366,3 +369,24 @@ def test_fast_exp_matches_exp_double_on_every_float(ops, cuda):
     inside = 2 * (bits(80.0) + 1)
     outside = total - inside
     assert slow - outside < 1e-4 * inside
+
+
+def test_bounded_wait_gives_up_and_reports(ops, cuda):
+    """The bounded shared-memory barrier wait of the bulk-copy kernels, on a
+    barrier nothing completes: it gives up after its limit, the kernel
+    returns, B2_CHECK_WAIT is reported, and the context keeps working."""
+    import time
+
+    import torch
+
+    from aps2026_b200 import _lib
+
+    ops.device_status()
+    t0 = time.perf_counter()
+    assert _lib.lib().b2_selfcheck_wait(20_000_000) == 0  # 20 ms
+    assert ops.device_status() & 32
+    assert time.perf_counter() - t0 < 5.0
+    a, b = torch.ones(1000, device=cuda), torch.ones(1000, device=cuda)
+    ops.add_inplace_gpu(a, b)
+    torch.cuda.synchronize()
+    assert float(a[0]) == 2.0
