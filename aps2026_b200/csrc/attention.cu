@@ -508,7 +508,7 @@ struct BlockAttention {
                     acc[0][3][0] = __fmaf_rn(pa.w, vv.x, acc[0][3][0]); acc[0][3][1] = __fmaf_rn(pa.w, vv.y, acc[0][3][1]);
                 }
                 const int e2 = min(w1a, w1b);
-#pragma unroll 4
+#pragma unroll 8
                 for (int w = max(w0a, w0b); w <= e2; ++w) {  // both rows
                     const float4 pa = *reinterpret_cast<const float4*>(prow + w * kCombos);
                     const float4 pb = *reinterpret_cast<const float4*>(prow + w * kCombos + 4);
