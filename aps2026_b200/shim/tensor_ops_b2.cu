@@ -4,8 +4,9 @@
 // A maintainer adds this file to the reference build, links
 // libaps2026_b200.so, and deletes the functions defined here from
 // src/tensor.cu (add_inplace_gpu, silu_mul_gpu, layer_norm_gpu,
-// add_layer_norm_gpu, apply_rope_gpu, apply_rope_tree_gpu, both
-// gather_rows_gpu overloads). src/layer.cu, src/model.cu and src/main.cpp
+// add_layer_norm_gpu, apply_rope_gpu, apply_rope_tree_gpu, attention_gpu,
+// attention_tree_gpu, both gather_rows_gpu overloads). src/layer.cu,
+// src/model.cu and src/main.cpp
 // compile unchanged: same signatures, same Tensor handling (inputs through
 // cuda_data(), outputs through cuda_data_write(), the legacy default
 // stream), and the same exception types with the reference's messages
@@ -106,6 +107,43 @@ const std::uint32_t* packed_positions(const std::vector<std::size_t>& lens, std:
     return pos;
 }
 
+// The packed-segment layout of attention_gpu in the compact chain form of
+// b2_attention_tree_compact: segment b's rows offsets[b] .. offsets[b + 1]
+// are their own chain, so row r's keys are rows offsets[seg[r]] .. + pos
+// (token_node = identity). Cached per seq_lens like packed_positions.
+struct SegmentChains {
+    std::uint32_t* seg = nullptr;       // [rows] segment of each row
+    std::uint32_t* offsets = nullptr;   // [segments + 1]
+    std::uint32_t* identity = nullptr;  // [rows]
+};
+
+const SegmentChains& segment_chains(const std::vector<std::size_t>& lens) {
+    static std::vector<std::size_t> key;
+    static SegmentChains c;
+    if (c.seg && key == lens) return c;
+    for (std::uint32_t* p : {c.seg, c.offsets, c.identity})
+        if (p) cudaFree(p);
+    c = SegmentChains{};
+    std::vector<std::uint32_t> seg, offsets{0}, identity;
+    for (std::size_t b = 0; b < lens.size(); ++b) {
+        for (std::size_t p = 0; p < lens[b]; ++p) {
+            seg.push_back(static_cast<std::uint32_t>(b));
+            identity.push_back(static_cast<std::uint32_t>(identity.size()));
+        }
+        offsets.push_back(static_cast<std::uint32_t>(identity.size()));
+    }
+    auto upload = [](const std::vector<std::uint32_t>& h, std::uint32_t** d, const char* what) {
+        if (h.empty()) return;
+        cuda_check(cudaMalloc(d, h.size() * sizeof(std::uint32_t)), what);
+        cuda_check(cudaMemcpy(*d, h.data(), h.size() * sizeof(std::uint32_t), cudaMemcpyHostToDevice), what);
+    };
+    upload(seg, &c.seg, "segment chains: rows");
+    upload(offsets, &c.offsets, "segment chains: offsets");
+    upload(identity, &c.identity, "segment chains: identity");
+    key = lens;
+    return c;
+}
+
 // Staging for the std::vector gather overload (the reference's
 // device_rows(), src/tensor.cu:2739-2753).
 const std::uint32_t* device_rows(const std::vector<std::size_t>& rows) {
@@ -180,6 +218,34 @@ void apply_rope_tree_gpu(Tensor& q, Tensor& k, const std::uint32_t* row_pos, std
     check(b2_rope(q.cuda_data_write(), k.cuda_data_write(), row_pos, rows, q_heads, kv_heads, head_dim, t.cosine,
                   t.sine, t.max_seq, nullptr),
           "k_rope(tree) launch");
+}
+
+// GQA-4 (the model's layout) runs the prefix-tree kernel over segment chains,
+// whose arithmetic is k_attention_grouped_gqa4's; other head groupings
+// (the reference's k_attention) are not implemented here.
+void attention_gpu(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& out,
+                   const std::vector<std::size_t>& seq_lens, std::size_t q_heads, std::size_t kv_heads,
+                   std::size_t head_dim) {
+    if (q_heads != 4 * kv_heads)
+        throw std::invalid_argument("attention_gpu: only GQA-4 is implemented by the B200 library");
+    std::size_t rows = 0, max_seq = 0;
+    const std::uint32_t* pos = packed_positions(seq_lens, &rows, &max_seq);
+    if (rows == 0) return;
+    const SegmentChains& c = segment_chains(seq_lens);
+    check(b2_attention_tree_compact(q.cuda_data(), k.cuda_data(), v.cuda_data(), out.cuda_data_write(), pos, c.seg,
+                                    c.offsets, seq_lens.size(), c.identity, rows, max_seq, rows, q_heads, kv_heads,
+                                    head_dim, apss26::SLIDING_WINDOW, kFlags, nullptr),
+          "k_attention_grouped_gqa4 launch");
+}
+
+void attention_tree_gpu(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& out,
+                        const std::uint32_t* row_pos, const std::uint32_t* anc, std::size_t anc_stride,
+                        std::size_t rows, std::size_t max_seq, std::size_t q_heads, std::size_t kv_heads,
+                        std::size_t head_dim) {
+    (void)max_seq;  // positions are bounded by anc_stride
+    check(b2_attention_tree(q.cuda_data(), k.cuda_data(), v.cuda_data(), out.cuda_data_write(), row_pos, anc,
+                            anc_stride, rows, q_heads, kv_heads, head_dim, apss26::SLIDING_WINDOW, kFlags, nullptr),
+          "k_attention_tree_gqa4 launch");
 }
 
 void gather_rows_gpu(const Tensor& x, const std::vector<std::size_t>& rows, Tensor& out) {

@@ -91,6 +91,7 @@ def ref() -> C.CDLL:
             "ref_k_add": [_vp, _vp, _sz, _vp],
             "ref_k_moe_gather_compact": [_vp, _vp, _vp, _sz, _sz, _vp],
             "ref_k_attention_tree": [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz, _sz, _sz, _vp],
+            "ref_k_attention_grouped": [_vp] * 6 + [_sz] * 5 + [_vp],
             "ref_sliding_window": [],
             "ref_cpu_layer_norm": [_vp, _vp, _vp, _vp, _sz, _sz, _f32, _vp],
             "ref_cpu_apply_rope": [_vp, _vp, _vp, _sz, _sz, _sz, _sz, _f32, _vp],

@@ -169,6 +169,27 @@ int ref_k_attention_tree(const float* q, const float* k, const float* v,
     return launch_status();
 }
 
+// k_attention_grouped_gqa4 with the launch of attention_gpu
+// (src/tensor.cu:3316-3330): seg_offset[r] is the first row of row r's
+// segment, seg_pos[r] its position in it.
+int ref_k_attention_grouped(const float* q, const float* k, const float* v, float* out,
+                            const std::uint32_t* seg_offset, const std::uint32_t* seg_pos, std::size_t rows,
+                            std::size_t max_seq, std::size_t q_heads, std::size_t kv_heads, std::size_t head_dim,
+                            void* stream) {
+    const std::size_t shared =
+        (4 * max_seq + 4 * head_dim + tensor_ops::ATTN_KEY_TILE * (head_dim + 1)) * sizeof(float);
+    if (shared > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(
+            tensor_ops::k_attention_grouped_gqa4,
+            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
+        if (e != cudaSuccess) return static_cast<int>(e);
+    }
+    tensor_ops::k_attention_grouped_gqa4<<<static_cast<unsigned>(rows * kv_heads), 128, shared,
+                                           as_stream(stream)>>>(
+        q, k, v, out, seg_offset, seg_pos, rows, q_heads, kv_heads, head_dim, max_seq);
+    return launch_status();
+}
+
 int ref_sliding_window(void) { return static_cast<int>(apss26::SLIDING_WINDOW); }
 
 // ---- host ops of the reference (host pointers) -----------------------------

@@ -155,3 +155,37 @@ def test_attention_tree_compact_chains_match_dense(cuda, hd):
     ops.attention_tree_compact_gpu(qd, kd, vd, compact, pos, bad, offs_d, dt.token_node, stride, R, 16, 4, hd, 2047)
     assert ops.device_status() & 8
     assert torch.equal(compact[deep], torch.zeros_like(compact[deep]))
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref/libref.so not built")
+def test_packed_segments_match_reference_grouped_kernel(cuda):
+    """attention_gpu's packed-segment attention (k_attention_grouped_gqa4) is
+    the compact-chain kernel with token_node = identity and one chain per
+    segment -- the mapping the C++ shim uses; bit-exact to the reference."""
+    import torch
+
+    from aps2026_b200 import ops
+
+    lens = [300, 5, 129, 1, 64]
+    rows = sum(lens)
+    offs = np.zeros(len(lens) + 1, np.int32)
+    offs[1:] = np.cumsum(lens)
+    seg = np.repeat(np.arange(len(lens), dtype=np.int32), lens)
+    pos = np.concatenate([np.arange(n, dtype=np.int32) for n in lens])
+    base = offs[:-1][seg]
+    g = rng(55)
+    q, k, v = normal(g, (rows, 16 * 128)), normal(g, (rows, 4 * 128)), normal(g, (rows, 4 * 128))
+    qd, kd, vd = to_dev(q, cuda), to_dev(k, cuda), to_dev(v, cuda)
+    ref = torch.full((rows, 16 * 128), float("nan"), device=cuda)
+    st = torch.cuda.current_stream().cuda_stream
+    base_d, pos_d = to_dev(base, cuda), to_dev(pos, cuda)  # alive until the kernels have run
+    rc = oracle.ref().ref_k_attention_grouped(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), ref.data_ptr(),
+                                              base_d.data_ptr(), pos_d.data_ptr(), rows, max(lens), 16, 4, 128, st)
+    assert rc == 0
+    out = torch.full_like(ref, float("nan"))
+    ident = torch.arange(rows, dtype=torch.int32, device=cuda)
+    seg_d, offs_d = to_dev(seg, cuda), to_dev(offs, cuda)
+    ops.attention_tree_compact_gpu(qd, kd, vd, out, pos_d, seg_d, offs_d, ident, max(lens), rows, 16, 4, 128,
+                                   exact=True)
+    torch.cuda.synchronize()
+    oracle.assert_bitexact(to_host(out), to_host(ref), "compact chains vs k_attention_grouped_gqa4")

@@ -22,6 +22,10 @@ EXPECTED = {
     "tensor_ops::gather_rows_gpu(Tensor const&, std::vector<unsigned long, std::allocator<unsigned long> > const&, "
     "Tensor&)",
     "tensor_ops::gather_rows_gpu(Tensor const&, tensor_ops::RowIndexBuffer const&, Tensor&)",
+    "tensor_ops::attention_gpu(Tensor const&, Tensor const&, Tensor const&, Tensor&, "
+    "std::vector<unsigned long, std::allocator<unsigned long> > const&, unsigned long, unsigned long, unsigned long)",
+    "tensor_ops::attention_tree_gpu(Tensor const&, Tensor const&, Tensor const&, Tensor&, unsigned int const*, "
+    "unsigned int const*, unsigned long, unsigned long, unsigned long, unsigned long, unsigned long, unsigned long)",
 }
 
 
