@@ -12,11 +12,13 @@
  *     explicit sizes -- shapes that the reference read from Tensor::size();
  *   - every device entry point takes the stream to run on (NULL = legacy
  *     default stream, which is what the reference always used);
- *   - nothing allocates device memory; scratch is caller-provided and sized by
- *     a *_workspace_size() query;
+ *   - no hot-path entry point allocates device memory; scratch is
+ *     caller-provided and sized by a *_workspace_size() query (the
+ *     diagnostic b2_selfcheck_exp allocates a 24-byte counter block);
  *   - there is no hidden per-process state except one status word per device
- *     that in-kernel bounds checks write (b2_device_status), so one host
- *     thread per GPU may call concurrently on different devices/streams;
+ *     that in-kernel bounds checks write (b2_device_status) and the fixed
+ *     scratch of b2_moe_route_noalloc, so one host thread per GPU may call
+ *     concurrently on different devices/streams;
  *   - errors are status codes instead of the reference's exceptions:
  *     B2_ERR_INVALID_ARGUMENT where the reference throws
  *     std::invalid_argument, B2_ERR_CUDA where its check_cuda throws
