@@ -1,0 +1,66 @@
+"""Config 5 at full size (64 prompts x 2048 tokens = 131,072 trie rows, 32
+layers, hidden 4096) through b2_prefill_layers, checked by properties that
+do not need the CPU oracle to rerun the whole batch:
+  - the final LayerNorm of sampled rows equals the oracle's serial-order
+    LayerNorm of the same GPU-produced residual rows, bit for bit
+    (B2_FLAG_EXACT_ORDER);
+  - the last layer's routing left in the pipeline's buffers equals the
+    oracle's routing of that layer's logits for all 131,072 tokens;
+  - two runs on identical inputs give identical outputs;
+  - the default tree-order reductions agree with the exact order within the
+    north_star tolerance."""
+import numpy as np
+import pytest
+
+import oracle
+from tests._util import to_host
+
+pytestmark = pytest.mark.gpu
+
+
+def test_config5_full_size_properties(cuda):
+    import torch
+
+    from aps2026_b200 import prefill
+
+    prompts = prefill.prompts_config5()
+    batch = prefill.Batch.build(prompts, cuda)
+    assert batch.rows == 64 * 2048
+    w = prefill.Weights.make(cuda, seed=4, layers=32)
+
+    def run(exact):
+        gen = torch.Generator(device=cuda).manual_seed(77)  # the same stand-ins every run
+        sets = [prefill.StandIns.make(batch.rows, cuda, gen) for _ in range(2)]
+        pipe = prefill.Pipeline(batch, w, cuda, exact=exact)
+        pipe.bind_layers(sets, 32)
+        pipe.run()
+        torch.cuda.synchronize()
+        return pipe, sets
+
+    pipe, sets = run(exact=True)
+    sample = torch.from_numpy(np.random.default_rng(5).choice(batch.rows, 256, replace=False)).to(cuda)
+    fx = to_host(pipe.final_x[sample])
+    fy = to_host(pipe.final_out[sample])
+    want = oracle.layer_norm(fx, to_host(w.final[0]), to_host(w.final[1]))
+    oracle.assert_bitexact(fy, want, "config 5: final LayerNorm of sampled rows")
+
+    r = oracle.moe_route(to_host(sets[31 % 2].logits))  # layer 31's logits (read-only stand-in)
+    oracle.assert_bitexact(to_host(pipe.routing.assignment_rows).view(np.uint32), r["assignment_rows"],
+                           "config 5: last layer's assignment rows")
+    oracle.assert_bitexact(to_host(pipe.routing.route_positions).view(np.uint32), r["route_positions"],
+                           "config 5: last layer's route positions")
+    exact_out = pipe.final_out[sample].clone()
+    exact_x = pipe.final_x[sample].clone()
+    del pipe, sets
+    torch.cuda.empty_cache()
+
+    again, sets = run(exact=True)
+    assert torch.equal(again.final_out[sample], exact_out) and torch.equal(again.final_x[sample], exact_x)
+    del again, sets
+    torch.cuda.empty_cache()
+
+    tree, sets = run(exact=False)
+    assert torch.equal(tree.final_x[sample], exact_x)  # the residual stream is elementwise: same bits
+    oracle.assert_close(to_host(tree.final_out[sample]), to_host(exact_out), what="config 5: tree vs exact order")
+    del tree, sets
+    torch.cuda.empty_cache()
