@@ -340,6 +340,127 @@ ln_rows_bulk(LnArgs a) {
     }
 }
 
+// Reference-order (B2_FLAG_EXACT_ORDER) LayerNorm of many rows (plain
+// LayerNorm; the fused-add forms keep the per-row kernel, which measured
+// faster with their second and third input streams). The serial sums are 2h
+// dependent additions per row; issued one row per thread they leave 31 of a
+// warp's lanes idle. Here a CTA takes 32 rows at a time and warp 0 runs the
+// 32 rows' chains side by side, lane r summing row r's staged chunk in
+// ascending order, while the other 15 warps stage the next chunk
+// (kExactChunk floats of each row) into the other shared buffer with
+// coalesced 128-bit loads, 8 in flight per thread. Pass A forms the sums,
+// pass B the squared deviations (re-reading the 32 rows, which one CTA per
+// SM keeps within L2), pass C writes y with every thread. Same operations in
+// the same order as serial_moments, so the output is bit-identical to the
+// reference.
+constexpr int kExactRows = 32;
+constexpr int kExactChunk = 512;
+constexpr int kExactPitch = kExactChunk + 4;  // floats; spreads the lanes' rows over the banks
+constexpr int kExactThreads = 512;
+
+__global__ void __launch_bounds__(kExactThreads, 1)
+ln_exact_batch(LnArgs a) {
+    pdl_begin();
+    constexpr int THREADS = kExactThreads, LOADERS = THREADS - 32, U = 8;
+    extern __shared__ __align__(16) float stage_buf[];  // [2][kExactRows][kExactPitch]
+    __shared__ float mean_s[kExactRows], inv_s[kExactRows];
+    const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const std::size_t h = a.h, h4 = h / 4;
+    const int chunks = static_cast<int>((h + kExactChunk - 1) / kExactChunk);
+    const float hf = static_cast<float>(h);
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    for (std::size_t b0 = static_cast<std::size_t>(blockIdx.x) * kExactRows; b0 < a.rows;
+         b0 += static_cast<std::size_t>(gridDim.x) * kExactRows) {
+        const int nr = static_cast<int>(a.rows - b0 < kExactRows ? a.rows - b0 : kExactRows);
+        // copies chunk c of the batch's rows into buffer c & 1; each thread
+        // issues U loads before it stores any, so a chunk costs a few memory
+        // latencies, not one per item
+        auto stage = [&](int c, unsigned first, unsigned stride) {
+            const std::size_t c4 = static_cast<std::size_t>(c) * (kExactChunk / 4);
+            const unsigned len4 = static_cast<unsigned>(min(static_cast<std::size_t>(kExactChunk / 4), h4 - c4));
+            const unsigned total = static_cast<unsigned>(nr) * len4;
+            float4* buf = reinterpret_cast<float4*>(stage_buf + (c & 1) * kExactRows * kExactPitch);
+            for (unsigned it0 = first; it0 < total; it0 += stride * U) {
+                float4 v[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const unsigned it = it0 + u * stride;
+                    if (it < total) v[u] = ld_plain(x4 + (b0 + it / len4) * h4 + c4 + it % len4);
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const unsigned it = it0 + u * stride;
+                    if (it < total) buf[(it / len4) * (kExactPitch / 4) + it % len4] = v[u];
+                }
+            }
+        };
+        // lane r runs f over row r's elements of chunk c, in ascending order
+        auto chain = [&](int c, auto f) {
+            const std::size_t c4 = static_cast<std::size_t>(c) * (kExactChunk / 4);
+            const unsigned len4 = static_cast<unsigned>(min(static_cast<std::size_t>(kExactChunk / 4), h4 - c4));
+            const float4* row = reinterpret_cast<const float4*>(stage_buf + (c & 1) * kExactRows * kExactPitch +
+                                                                  lane * kExactPitch);
+#pragma unroll 4
+            for (unsigned i = 0; i < len4; ++i) {
+                const float4 v = row[i];
+                f(v.x);
+                f(v.y);
+                f(v.z);
+                f(v.w);
+            }
+        };
+        float acc = 0.0f, mean = 0.0f;
+        for (int pass = 0; pass < 2; ++pass) {
+            stage(0, tid, THREADS);
+            __syncthreads();
+            for (int c = 0; c < chunks; ++c) {
+                if (warp != 0) {
+                    if (c + 1 < chunks) stage(c + 1, tid - 32, LOADERS);
+                } else if (lane < static_cast<unsigned>(nr)) {
+                    if (pass == 0)
+                        chain(c, [&](float x) { acc = __fadd_rn(acc, x); });
+                    else
+                        chain(c, [&](float x) {
+                            const float t = __fsub_rn(x, mean);
+                            acc = __fmaf_rn(t, t, acc);
+                        });
+                }
+                __syncthreads();
+            }
+            if (pass == 0) {
+                mean = __fdiv_rn(acc, hf);
+                acc = 0.0f;
+            }
+        }
+        if (warp == 0 && lane < static_cast<unsigned>(nr)) {
+            mean_s[lane] = mean;
+            inv_s[lane] = inv_std(acc, hf, a.eps);
+        }
+        __syncthreads();
+        // ---- pass C: y for the batch, all threads, coalesced ----
+        const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+        const float4* be4 = reinterpret_cast<const float4*>(a.beta);
+        const std::size_t total = static_cast<std::size_t>(nr) * h4;
+        for (std::size_t it0 = tid; it0 < total; it0 += THREADS * U) {
+            float4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {  // all loads first
+                const std::size_t it = it0 + static_cast<std::size_t>(u) * THREADS;
+                if (it < total) v[u] = ld_plain(x4 + b0 * h4 + it);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const std::size_t it = it0 + static_cast<std::size_t>(u) * THREADS;
+                if (it >= total) continue;
+                const std::size_t r = it / h4, j = it % h4;
+                st_plain(reinterpret_cast<float4*>(a.y) + b0 * h4 + it,
+                         ln_out4(v[u], mean_s[r], inv_s[r], __ldg(g4 + j), __ldg(be4 + j)));
+            }
+        }
+        __syncthreads();  // mean_s / inv_s and the buffers are reused by the next batch
+    }
+}
+
 constexpr std::size_t kMaxSmemRow = 220 * 1024;  // + static reduction slots <= 227 KB
 
 template <int MODE, int THREADS, int V, bool EXACT>
@@ -350,6 +471,16 @@ int launch_reg(const LnArgs& a, cudaStream_t s) {
         return launch_result("layer norm: shared memory attribute");
     const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), THREADS, smem, a.rows);
     launch_pdl(kernel, grid, THREADS, smem, s, a);
+    return B2_OK;
+}
+
+int launch_exact_batch(const LnArgs& a, cudaStream_t s) {
+    const std::size_t smem = 2 * kExactRows * kExactPitch * sizeof(float);
+    if (allow_dynamic_smem(reinterpret_cast<const void*>(ln_exact_batch), smem) != cudaSuccess)
+        return launch_result("layer norm: shared memory attribute");
+    const std::size_t batches = (a.rows + kExactRows - 1) / kExactRows;
+    const unsigned grid = static_cast<unsigned>(batches < static_cast<std::size_t>(sm_count()) ? batches : sm_count());
+    launch_pdl(ln_exact_batch, grid, kExactThreads, smem, s, a);
     return B2_OK;
 }
 
@@ -376,16 +507,19 @@ int launch_smem(const LnArgs& a, cudaStream_t s) {
     return B2_OK;
 }
 
-// Picks the register-resident variant whose THREADS * V covers h / 4, else
-// bulk-copy staging (aligned rows, h % 4 == 0), else the scalar
-// shared-memory one.
+// Picks, for plain LayerNorm in reference order over at least 32 rows per
+// SM, the 32-row batched kernel; otherwise the register-resident variant
+// whose THREADS * V covers h / 4, else bulk-copy staging (aligned rows,
+// h % 4 == 0), else the scalar shared-memory one.
 template <int MODE>
 int dispatch(const LnArgs& a, bool exact, bool vec_ok, cudaStream_t s, const char* what) {
     if (a.h * sizeof(float) > kMaxSmemRow && exact)
         return set_error(B2_ERR_UNSUPPORTED, std::string(what) + ": h too large");
     int rc = B2_OK;
     const std::size_t h4 = a.h / 4;
-    if (vec_ok && !exact && h4 <= 256 * 8) {
+    if (MODE == kLN && vec_ok && exact && a.rows >= static_cast<std::size_t>(kExactRows) * sm_count()) {
+        rc = launch_exact_batch(a, s);  // enough rows for a 32-row batch on every SM
+    } else if (vec_ok && !exact && h4 <= 256 * 8) {
         if (h4 <= 256) rc = launch_reg<MODE, 256, 1, false>(a, s);
         else if (h4 <= 512) rc = launch_reg<MODE, 256, 2, false>(a, s);
         else if (h4 <= 1024) rc = launch_reg<MODE, 256, 4, false>(a, s);

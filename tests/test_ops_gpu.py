@@ -64,9 +64,11 @@ def test_gather_rows_empty_and_bad_index(ops, cuda):
 # ---- LayerNorm ----------------------------------------------------------------------
 
 # register rows (h <= 8192 tree order, <= 4096 exact order), bulk-copy staged
-# rows (aligned, h % 4 == 0, longer), scalar staged rows (h % 4 != 0)
+# rows (aligned, h % 4 == 0, longer), scalar staged rows (h % 4 != 0); in
+# exact order, plain LayerNorm over >= 32 rows per SM takes the 32-row batched
+# kernel (partial last batch, partial last chunk at h = 4100)
 LN_SHAPES = [(512, 4096), (7, 4096), (3, 100), (5, 4100), (2, 12288), (1, 8192), (4, 2048), (3, 16384),
-             (2, 37)]
+             (2, 37), (4800, 4096), (5003, 4100)]
 
 
 @pytest.mark.parametrize("rows,h", LN_SHAPES)
@@ -305,7 +307,7 @@ def test_moe_combine_bitexact(ops, cuda, T, h):
     oracle.assert_bitexact(to_host(out), oracle.moe_combine(eo, r["routes"], r["route_positions"], T), "combine")
 
 
-@pytest.mark.parametrize("T,h", [(4096, 4096), (5, 100), (3, 12288), (6, 8192)])
+@pytest.mark.parametrize("T,h", [(4096, 4096), (5, 100), (3, 12288), (6, 8192), (4801, 4096)])
 @pytest.mark.parametrize("exact", [False, True])
 def test_moe_combine_add_layer_norm(ops, cuda, T, h, exact):
     import torch
