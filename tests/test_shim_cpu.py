@@ -39,3 +39,24 @@ def test_shim_compiles_against_reference_headers(tmp_path):
     defined = {line.split(" T ", 1)[1] for line in nm.splitlines() if " T tensor_ops::" in line
                and "(anonymous namespace)" not in line}
     assert defined == EXPECTED
+
+
+DROPIN_B2 = ROOT / "oracle" / "_ref" / "libdropin_b2.so"
+
+
+@pytest.mark.skipif(not DROPIN_B2.exists(), reason="drop-in library not built (needs the reference tree)")
+def test_dropin_library_takes_the_shim_functions():
+    """oracle/_ref/libdropin_b2.so (the reference model code with the shim in
+    place of the replaced tensor_ops functions): each replaced function is
+    defined once under its own name (the shim's) and once renamed out of the
+    reference's tensor.cu, and the shim's calls go to libaps2026_b200.so."""
+    nm = subprocess.run(["nm", "-C", "--defined-only", str(DROPIN_B2)], capture_output=True, text=True,
+                        check=True).stdout
+    defined = {line.split(" T ", 1)[1] for line in nm.splitlines() if " T tensor_ops::" in line}
+    for sig in EXPECTED:
+        assert sig in defined
+        assert sig.replace("tensor_ops::", "tensor_ops::ref_replaced_", 1) in defined
+    undefined = subprocess.run(["nm", "-u", str(DROPIN_B2)], capture_output=True, text=True, check=True).stdout
+    assert "b2_layer_norm" in undefined and "b2_attention_tree_compact" in undefined
+    needed = subprocess.run(["readelf", "-d", str(DROPIN_B2)], capture_output=True, text=True, check=True).stdout
+    assert "libaps2026_b200.so" in needed
