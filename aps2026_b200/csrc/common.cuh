@@ -152,6 +152,28 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
+// Completes the barrier's phase with no bytes expected (a slot whose copy
+// was skipped keeps its phase count in step).
+__device__ __forceinline__ void mbar_arrive(std::uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// 1-D bulk copy shared -> global, in this thread's current bulk group.
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, unsigned bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_addr(src)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N of this thread's bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N of this thread's bulk groups are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
 // Waits for the barrier phase of parity `parity`; false if it did not
 // complete within `limit_ns` (or kMbarMaxPolls polls).
 __device__ __forceinline__ bool mbar_wait(std::uint64_t* bar, unsigned parity,

@@ -32,7 +32,11 @@ def _sync():
 # ---- gather -------------------------------------------------------------------
 
 
-@pytest.mark.parametrize("vocab,h,count", [(32064, 4096, 512), (1000, 4096, 1), (97, 37, 50), (64, 4100, 33)])
+# register-staged rows (h < 1024 or unaligned) and bulk-copy rows (one 16 KB
+# chunk at h = 4096; two at h = 5000; many units per CTA at 20,000 rows)
+@pytest.mark.parametrize("vocab,h,count", [(32064, 4096, 512), (1000, 4096, 1), (97, 37, 50), (64, 4100, 33),
+                                           (300, 5000, 777), (4000, 1024, 3001), (32064, 4096, 20000),
+                                           (50, 1020, 9)])
 def test_gather_rows_bitexact(ops, cuda, vocab, h, count):
     import torch
 
@@ -45,18 +49,19 @@ def test_gather_rows_bitexact(ops, cuda, vocab, h, count):
     oracle.assert_bitexact(to_host(out), oracle.gather_rows(emb, rows), "gather")
 
 
-def test_gather_rows_empty_and_bad_index(ops, cuda):
+@pytest.mark.parametrize("h", [64, 4096, 5000])
+def test_gather_rows_empty_and_bad_index(ops, cuda, h):
     import torch
 
-    emb = torch.randn(10, 64, device=cuda)
-    out = torch.full((3, 64), 7.0, device=cuda)
+    emb = torch.randn(10, h, device=cuda)
+    out = torch.full((3, h), 7.0, device=cuda)
     ops.gather_rows_gpu(emb, torch.zeros(0, dtype=torch.int32, device=cuda), out[:0])
     assert ops.device_status() == 0
     rows = torch.tensor([1, 10, 2], dtype=torch.int32, device=cuda)  # 10 is out of range
     ops.gather_rows_gpu(emb, rows, out)
     status = ops.device_status()
     assert status & 1, "out-of-range index not reported"
-    assert torch.equal(out[1], torch.zeros(64, device=cuda))
+    assert torch.equal(out[1], torch.zeros(h, device=cuda))
     assert torch.equal(out[0], emb[1]) and torch.equal(out[2], emb[2])
     assert ops.device_status() == 0, "status word not cleared"
 
