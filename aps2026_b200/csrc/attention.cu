@@ -17,9 +17,10 @@
 //     stored), every thread computing one key for two of the four query
 //     heads from 128-bit shared reads -- the four accumulators over d mod 4
 //     and their (a0 + a1) + (a2 + a3) combination are the reference's;
-//   - softmax: a warp per query head (max by shuffles, the exponential of
-//     fastexp.cuh, the denominator serially by one lane in EXACT_ORDER or
-//     by a shuffle tree otherwise, Markstein division);
+//   - softmax: a warp per query head (max by shuffles; in EXACT_ORDER the
+//     reference's exponential (fastexp.cuh), the denominator serially by one
+//     lane and Markstein division; otherwise CUDA's expf, a shuffle-tree
+//     denominator and a multiplication by its reciprocal);
 //   - values: tiles of 64 rows staged like the keys, each thread owning one
 //     output dimension and accumulating the four heads in ascending key
 //     order with fused multiply-adds, reading p[w][0..3] as one 128-bit
@@ -67,8 +68,11 @@ __device__ __forceinline__ const std::uint32_t* chain_of(const AttnArgs& a, std:
 }
 
 // Division by a row denominator d >= 1 with one reciprocal per row, as in
-// softmax.cu (Markstein's correction gives the correctly rounded quotient).
+// softmax.cu (in EXACT_ORDER Markstein's correction gives the correctly
+// rounded quotient).
+template <bool EXACT>
 __device__ __forceinline__ float attn_div(float e, float d, float y) {
+    if (!EXACT) return __fmul_rn(e, y);  // tree-order mode: within 1.5 ulp
     if (e < 0x1p-96f) return __fdiv_rn(e, d);
     const float q = __fmul_rn(e, y);
     return __fmaf_rn(__fmaf_rn(-d, q, e), y, q);
@@ -185,7 +189,7 @@ attention_tree_kernel(AttnArgs a) {
         m = warp_max(m);
         float part = 0.0f;
         for (int w = lane; w < W; w += 32) {
-            const float e = exp_ref(__fsub_rn(scores[w * kGroup + g], m), tab);
+            const float e = exp_mode<EXACT>(__fsub_rn(scores[w * kGroup + g], m), tab);
             scores[w * kGroup + g] = e;
             part = __fadd_rn(part, e);
         }
@@ -200,7 +204,7 @@ attention_tree_kernel(AttnArgs a) {
             denom = warp_sum(part);
         }
         const float y = __frcp_rn(denom);
-        for (int w = lane; w < W; w += 32) scores[w * kGroup + g] = attn_div(scores[w * kGroup + g], denom, y);
+        for (int w = lane; w < W; w += 32) scores[w * kGroup + g] = attn_div<EXACT>(scores[w * kGroup + g], denom, y);
     }
     __syncthreads();
 
@@ -439,7 +443,7 @@ struct BlockAttention {
             __syncthreads();  // red is reused
             float part = 0.0f;
             for (int w = wb + par; w <= we; w += 2) {
-                const float e = exp_ref(__fsub_rn(scores[w * kCombos + c], m), tab);
+                const float e = exp_mode<EXACT>(__fsub_rn(scores[w * kCombos + c], m), tab);
                 scores[w * kCombos + c] = e;
                 part = __fadd_rn(part, e);
             }
@@ -464,7 +468,7 @@ struct BlockAttention {
             }
             const float y = __frcp_rn(d);
             for (int w = wb + par; w <= we; w += 2)
-                scores[w * kCombos + c] = attn_div(scores[w * kCombos + c], d, y);
+                scores[w * kCombos + c] = attn_div<EXACT>(scores[w * kCombos + c], d, y);
         }
 
         // ---- out[r][h][d] = sum_w p[w][r * 4 + h] v[w][d], ascending w ----

@@ -39,6 +39,12 @@ __host__ __device__ inline bool aligned16(const void* p) {
 // Number of SMs of the current device (148 on B200), cached per device.
 int sm_count();
 
+// Gated SiLU launch (moe.cu) with the exponential mode chosen by the caller:
+// b2_silu_mul passes exact = true (bit-exact always); b2_prefill_layers the
+// mode of its flags.
+int silu_mul_launch(const float* gate, std::size_t ld_gate, const float* up, std::size_t ld_up, float* out,
+                    std::size_t ld_out, std::size_t rows, std::size_t cols, bool exact, b2_stream_t stream);
+
 // Resident CTAs per SM for `kernel` at `threads` threads and `smem` bytes of
 // dynamic shared memory on the current device.
 int resident_ctas(const void* kernel, int threads, std::size_t smem);

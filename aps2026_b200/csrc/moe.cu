@@ -316,14 +316,15 @@ route_scatter(RouteArgs a) {
 
 // ---- gated SiLU -------------------------------------------------------------
 
-// g / (1 + (float)exp((double)-g)) * u, k_silu_mul (src/tensor.cu:2005-2008);
-// the exponential bit-identical through exp_ref (fastexp.cuh).
-__device__ __forceinline__ float silu_from_exp(float g, float u, float e) {
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
-}
-
+// g / (1 + (float)exp((double)-g)) * u, k_silu_mul (src/tensor.cu:2005-2008):
+// EXACT bit for bit (exp_ref of fastexp.cuh and an IEEE division); the
+// tree-order mode of b2_prefill_layers uses CUDA's expf and __fdividef
+// (within 2 ulp each: a few 1e-7 relative; a quotient whose denominator
+// exceeds 2^126 becomes 0 instead of |g| / (1 + e) < 1e-36).
+template <bool EXACT>
 __device__ __forceinline__ float silu_mul1(float g, float u, const double* tab) {
-    return silu_from_exp(g, u, exp_ref(-g, tab));
+    if (EXACT) return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g, tab))), u);
+    return __fmul_rn(__fdividef(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
 constexpr int kSiluThreads = 256;
@@ -335,14 +336,17 @@ constexpr int kSiluThreads = 256;
 // with four chunks per lane in flight measured 40% slower: the 448-column
 // rows leave a quarter of the lanes idle on the last chunk and the extra
 // registers halved the resident warps.)
+template <bool EXACT>
 __global__ void __launch_bounds__(kSiluThreads, 4)
 silu_mul_vec(const float* __restrict__ gate, std::size_t ldg, const float* __restrict__ up,
              std::size_t ldu, float* __restrict__ out, std::size_t ldo, std::size_t rows,
              std::size_t c4) {
     pdl_begin();
     __shared__ double tab[64];
-    load_exp2_table(tab);
-    __syncthreads();
+    if (EXACT) {
+        load_exp2_table(tab);
+        __syncthreads();
+    }
     // (row, chunk) of flat index i, advanced by the grid stride without a
     // division per step
     const std::size_t stride = static_cast<std::size_t>(gridDim.x) * kSiluThreads;
@@ -358,25 +362,28 @@ silu_mul_vec(const float* __restrict__ gate, std::size_t ldg, const float* __res
         const float4 g = ld_stream(reinterpret_cast<const float4*>(gate + r * ldg) + c);
         const float4 u = ld_stream(reinterpret_cast<const float4*>(up + r * ldu) + c);
         st_plain(reinterpret_cast<float4*>(out + r * ldo) + c,
-                 make_float4(silu_mul1(g.x, u.x, tab), silu_mul1(g.y, u.y, tab), silu_mul1(g.z, u.z, tab),
-                             silu_mul1(g.w, u.w, tab)));
+                 make_float4(silu_mul1<EXACT>(g.x, u.x, tab), silu_mul1<EXACT>(g.y, u.y, tab),
+                             silu_mul1<EXACT>(g.z, u.z, tab), silu_mul1<EXACT>(g.w, u.w, tab)));
     }
 }
 
+template <bool EXACT>
 __global__ void __launch_bounds__(kSiluThreads)
 silu_mul_scalar(const float* __restrict__ gate, std::size_t ldg, const float* __restrict__ up,
                 std::size_t ldu, float* __restrict__ out, std::size_t ldo, std::size_t rows,
                 std::size_t cols) {
     pdl_begin();
     __shared__ double tab[64];
-    load_exp2_table(tab);
-    __syncthreads();
+    if (EXACT) {
+        load_exp2_table(tab);
+        __syncthreads();
+    }
     const unsigned lane = threadIdx.x & 31;
     const std::size_t warps = static_cast<std::size_t>(gridDim.x) * (kSiluThreads / 32);
     for (std::size_t r = static_cast<std::size_t>(blockIdx.x) * (kSiluThreads / 32) + (threadIdx.x >> 5);
          r < rows; r += warps)
         for (std::size_t j = lane; j < cols; j += 32)
-            out[r * ldo + j] = silu_mul1(__ldg(gate + r * ldg + j), __ldg(up + r * ldu + j), tab);
+            out[r * ldo + j] = silu_mul1<EXACT>(__ldg(gate + r * ldg + j), __ldg(up + r * ldu + j), tab);
 }
 
 // ---- weighted un-permute ----------------------------------------------------
@@ -452,6 +459,30 @@ add_scalar(float* __restrict__ a, const float* __restrict__ b, std::size_t n) {
 std::size_t route_tiles(std::size_t T) { return (T + kTile - 1) / kTile; }
 
 }  // namespace
+
+int silu_mul_launch(const float* gate, std::size_t ld_gate, const float* up, std::size_t ld_up, float* out,
+                    std::size_t ld_out, std::size_t rows, std::size_t cols, bool exact, b2_stream_t stream) {
+    if (rows == 0 || cols == 0) return B2_OK;
+    if (!gate || !up || !out) return invalid("silu_mul: null pointer");
+    if (ld_gate < cols || ld_up < cols || ld_out < cols) return invalid("silu_mul shape");
+    cudaStream_t s = as_stream(stream);
+    const bool vec = (cols % 4) == 0 && (ld_gate % 4) == 0 && (ld_up % 4) == 0 && (ld_out % 4) == 0 &&
+                     aligned16(gate) && aligned16(up) && aligned16(out);
+    if (vec) {
+        auto kernel = exact ? silu_mul_vec<true> : silu_mul_vec<false>;
+        const std::size_t chunks = rows * (cols / 4);
+        const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), kSiluThreads, 0,
+                                        (chunks + kSiluThreads - 1) / kSiluThreads);
+        launch_pdl(kernel, grid, kSiluThreads, 0, s, gate, ld_gate, up, ld_up, out, ld_out, rows, cols / 4);
+    } else {
+        auto kernel = exact ? silu_mul_scalar<true> : silu_mul_scalar<false>;
+        const std::size_t blocks_needed = (rows + (kSiluThreads / 32) - 1) / (kSiluThreads / 32);
+        const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), kSiluThreads, 0, blocks_needed);
+        launch_pdl(kernel, grid, kSiluThreads, 0, s, gate, ld_gate, up, ld_up, out, ld_out, rows, cols);
+    }
+    return launch_result("b2_silu_mul");
+}
+
 }  // namespace b2
 
 B2_DEFINE_CHECK_TAKER(moe)
@@ -499,24 +530,7 @@ int b2_moe_route(const float* logits, size_t T, size_t E, float quantum, float t
 
 int b2_silu_mul(const float* gate, size_t ld_gate, const float* up, size_t ld_up, float* out,
                 size_t ld_out, size_t rows, size_t cols, b2_stream_t stream) {
-    using namespace b2;
-    if (rows == 0 || cols == 0) return B2_OK;
-    if (!gate || !up || !out) return invalid("silu_mul: null pointer");
-    if (ld_gate < cols || ld_up < cols || ld_out < cols) return invalid("silu_mul shape");
-    cudaStream_t s = as_stream(stream);
-    const bool vec = (cols % 4) == 0 && (ld_gate % 4) == 0 && (ld_up % 4) == 0 && (ld_out % 4) == 0 &&
-                     aligned16(gate) && aligned16(up) && aligned16(out);
-    const std::size_t blocks_needed = (rows + (kSiluThreads / 32) - 1) / (kSiluThreads / 32);
-    if (vec) {
-        const std::size_t chunks = rows * (cols / 4);
-        const unsigned grid = wave_grid(reinterpret_cast<const void*>(silu_mul_vec), kSiluThreads, 0,
-                                        (chunks + kSiluThreads - 1) / kSiluThreads);
-        launch_pdl(silu_mul_vec, grid, kSiluThreads, 0, s, gate, ld_gate, up, ld_up, out, ld_out, rows, cols / 4);
-    } else {
-        const unsigned grid = wave_grid(reinterpret_cast<const void*>(silu_mul_scalar), kSiluThreads, 0, blocks_needed);
-        launch_pdl(silu_mul_scalar, grid, kSiluThreads, 0, s, gate, ld_gate, up, ld_up, out, ld_out, rows, cols);
-    }
-    return launch_result("b2_silu_mul");
+    return b2::silu_mul_launch(gate, ld_gate, up, ld_up, out, ld_out, rows, cols, true, stream);
 }
 
 int b2_moe_combine(const float* expert_out, size_t expert_rows, const uint8_t* routes,

@@ -18,7 +18,7 @@
 //            [router logits = GEMM(post)]
 //   route(logits)                                      (b2_moe_route)
 //            [gate, up = grouped GEMM(post[assignment_rows])]
-//   act = silu(gate) * up                              (b2_silu_mul)
+//   act = silu(gate) * up      (b2_silu_mul; expf in the tree-order mode)
 //            [expert_out = grouped GEMM(act)]
 //   carry = attn
 // and finally x = combine(expert_out[L-1]) + carry, out = LN_final(x)
@@ -106,8 +106,8 @@ int b2_prefill_layers(const b2_prefill_shape* shape, const float* emb, size_t vo
                                work->route_ws_bytes, stream)))
             return rc;
         if ((rc = mark(stage + 2, 1)) || (rc = mark(stage + 3, 0))) return rc;
-        if ((rc = b2_silu_mul(L.gate, L.ld_gate_up, L.up, L.ld_gate_up, work->act, s.intermediate, 2 * rows,
-                              s.intermediate, stream)))
+        if ((rc = b2::silu_mul_launch(L.gate, L.ld_gate_up, L.up, L.ld_gate_up, work->act, s.intermediate,
+                                      2 * rows, s.intermediate, (flags & B2_FLAG_EXACT_ORDER) != 0, stream)))
             return rc;
         if ((rc = mark(stage + 3, 1))) return rc;
     }

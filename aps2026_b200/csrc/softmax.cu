@@ -13,10 +13,13 @@
 // exponentiated as the reference does ((float)exp((double)d), bit for bit,
 // through the table-driven exp_ref of fastexp.cuh), summed, divided
 // (Markstein: one correctly rounded reciprocal per row), and the full row
-// (zeros outside the window) written with 128-bit stores. Default:
-// tree-order denominator. B2_FLAG_EXACT_ORDER: the exponentials are staged
-// in shared memory and one thread sums them in ascending key order, as the
-// reference does, making the output bit-identical.
+// (zeros outside the window) written with 128-bit stores.
+// B2_FLAG_EXACT_ORDER: the exponentials are staged in shared memory and one
+// thread sums them in ascending key order, as the reference does, making
+// the output bit-identical. Default: tree-order denominator, CUDA's expf and
+// a multiplication by the row's rounded reciprocal (within the tolerance of
+// that mode; the bit-exact exponential is what makes the exact mode
+// issue-bound).
 // Algorithmic bytes: 4 * (window cells) read + 4 * T written per row. At
 // T = 2048 the exponential and division work, not HBM, sets the pace.
 #include "common.cuh"
@@ -43,7 +46,11 @@ struct SoftmaxArgs {
 // (Markstein's theorem, P. Markstein, IBM J. Res. Dev. 34(1), 1990). Three
 // FMA-pipe operations instead of a full division per element; arguments
 // below 2^-96, whose residual could leave the normal range, divide directly.
+// In the default (tree-order) mode the quotient is RN(e * y) instead, within
+// 1.5 ulp of e / d.
+template <bool EXACT>
 __device__ __forceinline__ float div_by_row(float e, float d, float y) {
+    if (!EXACT) return __fmul_rn(e, y);  // (y is NaN when d is)
     if (e < 0x1p-96f) return __fdiv_rn(e, d);  // (0 / NaN must stay NaN)
     const float q = __fmul_rn(e, y);
     const float r = __fmaf_rn(-d, q, e);
@@ -55,7 +62,7 @@ __device__ __forceinline__ float div_by_row(float e, float d, float y) {
 // the window [begin, i] are never read; inside read chunks, keys outside the
 // window hold -inf, whose exponential is +0 (no per-element masks in the
 // exponential or sum).
-template <int V>
+template <int V, bool EXACT>
 struct RowPart {
     float v[V][4];
     unsigned any = 0, full = 0;  // bit k: chunk k holds some / only window keys
@@ -93,7 +100,7 @@ struct RowPart {
             if ((any >> k) & 1u) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    v[k][e] = exp_ref(__fsub_rn(v[k][e], m), tab);
+                    v[k][e] = exp_mode<EXACT>(__fsub_rn(v[k][e], m), tab);
                     sum = __fadd_rn(sum, v[k][e]);
                 }
             } else {
@@ -112,11 +119,11 @@ struct RowPart {
             float pv[4] = {0.f, 0.f, 0.f, 0.f};
             if ((full >> k) & 1u) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) pv[e] = div_by_row(v[k][e], d, y);
+                for (int e = 0; e < 4; ++e) pv[e] = div_by_row<EXACT>(v[k][e], d, y);
             } else if ((any >> k) & 1u) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
-                    if (j0 + e >= begin && j0 + e <= i) pv[e] = div_by_row(v[k][e], d, y);
+                    if (j0 + e >= begin && j0 + e <= i) pv[e] = div_by_row<EXACT>(v[k][e], d, y);
             }
             st_plain(dst + c, make_float4(pv[0], pv[1], pv[2], pv[3]));
         }
@@ -142,7 +149,7 @@ causal_softmax_block(SoftmaxArgs a) {
         const std::size_t begin = i + 1 > a.window ? i + 1 - a.window : 0;
         const float4* src = reinterpret_cast<const float4*>(a.scores + row * a.ld);
         float4* dst = reinterpret_cast<float4*>(a.probs + row * a.ld);
-        RowPart<V> part;
+        RowPart<V, EXACT> part;
         const float m = block_max<WARPS>(part.load(src, threadIdx.x, THREADS, T4, begin, i, a.scale), red[0]);
         const float local_sum = part.exp_sum(m, tab);
         float denom;
@@ -196,7 +203,7 @@ causal_softmax_warp(SoftmaxArgs a) {
         const std::size_t begin = i + 1 > a.window ? i + 1 - a.window : 0;
         const float4* src = reinterpret_cast<const float4*>(a.scores + row * a.ld);
         float4* dst = reinterpret_cast<float4*>(a.probs + row * a.ld);
-        RowPart<V> part;
+        RowPart<V, EXACT> part;
         const float m = warp_max(part.load(src, lane, 32, T4, begin, i, a.scale));
         const float local_sum = part.exp_sum(m, tab);
         float denom;
@@ -246,7 +253,7 @@ causal_softmax_smem(SoftmaxArgs a) {
         const float m = block_max<kSmWarps>(local_max, red[0]);
         float local_sum = 0.0f;
         for (std::size_t j = begin + threadIdx.x; j <= i; j += kSmThreads) {
-            const float ex = exp_ref(__fsub_rn(staged[j], m), tab);
+            const float ex = exp_mode<EXACT>(__fsub_rn(staged[j], m), tab);
             staged[j] = ex;
             local_sum = __fadd_rn(local_sum, ex);
         }
@@ -265,7 +272,7 @@ causal_softmax_smem(SoftmaxArgs a) {
         }
         const float rden = __frcp_rn(denom);
         for (std::size_t j = threadIdx.x; j < a.T; j += kSmThreads)
-            dst[j] = (j >= begin && j <= i) ? div_by_row(staged[j], denom, rden) : 0.0f;
+            dst[j] = (j >= begin && j <= i) ? div_by_row<EXACT>(staged[j], denom, rden) : 0.0f;
         __syncthreads();
     }
 }

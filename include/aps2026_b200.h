@@ -26,10 +26,16 @@
  *     message of the calling thread's last failure.
  *
  * Floating point: by default reductions (LayerNorm moments, softmax
- * denominators) are tree-shaped and agree with the reference kernels within
- * 1e-5 relative OR 1e-6 absolute. With B2_FLAG_EXACT_ORDER they are
- * evaluated in the reference's serial ascending order and agree bit for bit.
- * Index/integer outputs (gather, routing, permutation) are always bit-exact.
+ * denominators) are tree-shaped, the softmax (and, inside
+ * b2_prefill_layers, the SiLU) exponentials are CUDA's expf and their
+ * quotients a multiplication by a rounded reciprocal, and results agree with
+ * the reference kernels within 1e-5 relative OR 1e-6 absolute. With
+ * B2_FLAG_EXACT_ORDER reductions run in the reference's serial ascending
+ * order, exponentials are the reference's (float)exp((double)x) and
+ * divisions correctly rounded, and results agree bit for bit. Functions
+ * without a flags argument (b2_silu_mul, b2_rope, b2_moe_combine, b2_add)
+ * are always bit-exact. Index/integer outputs (gather, routing,
+ * permutation) are always bit-exact.
  */
 #ifndef APS2026_B200_H
 #define APS2026_B200_H

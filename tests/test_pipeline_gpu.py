@@ -54,6 +54,15 @@ def test_pipeline_small_shared_prefix(cuda, exact):
         oracle.assert_bitexact(to_host(pipe.final_out), want_y, "final LayerNorm")
     else:
         oracle.assert_close(to_host(pipe.final_out), want_y, what="final LayerNorm")
+    # the last layer's gated SiLU (its output feeds only the stand-in expert
+    # GEMM): bit-exact in exact order, within tolerance with expf
+    inter = pipe.act.shape[1]
+    gu = host[(3 - 1) % 2]["gate_up"]
+    want_act = oracle.silu_mul(gu[:, :inter], gu[:, inter:])
+    if exact:
+        oracle.assert_bitexact(to_host(pipe.act), want_act, "SiLU")
+    else:
+        oracle.assert_close(to_host(pipe.act), want_act, what="SiLU")
     # the in-place updates of the stand-ins (RoPE on q/k; attn += x) agree too
     for s, h in zip(standins, host):
         oracle.assert_bitexact(to_host(s.q), h["q"], "rope q")
