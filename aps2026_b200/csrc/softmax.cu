@@ -67,13 +67,14 @@ struct RowPart {
     float v[V][4];
     unsigned any = 0, full = 0;  // bit k: chunk k holds some / only window keys
 
-    // Loads and scales the chunks; returns the thread's max score.
-    __device__ __forceinline__ float load(const float4* src, std::size_t first, std::size_t stride,
-                                          std::size_t T4, std::size_t begin, std::size_t i, float scale) {
+    // Loads and scales the chunks; returns the thread's max score. (Column
+    // indices are 32-bit: T * 4 bytes fits the shared-memory row limit.)
+    __device__ __forceinline__ float load(const float4* src, unsigned first, unsigned stride, unsigned T4,
+                                          unsigned begin, unsigned i, float scale) {
         float mx = -3.402823466e+38F;
 #pragma unroll
         for (int k = 0; k < V; ++k) {
-            const std::size_t c = first + static_cast<std::size_t>(k) * stride, j0 = 4 * c;
+            const unsigned c = first + static_cast<unsigned>(k) * stride, j0 = 4 * c;
             const bool a_k = c < T4 && j0 <= i && j0 + 3 >= begin;
             const bool f_k = a_k && j0 >= begin && j0 + 3 <= i;
             any |= static_cast<unsigned>(a_k) << k;
@@ -110,11 +111,11 @@ struct RowPart {
         return sum;
     }
     // dst chunk c_k <- v / d (zeros outside the window).
-    __device__ __forceinline__ void store(float4* dst, std::size_t first, std::size_t stride, std::size_t T4,
-                                          std::size_t begin, std::size_t i, float d, float y) const {
+    __device__ __forceinline__ void store(float4* dst, unsigned first, unsigned stride, unsigned T4,
+                                          unsigned begin, unsigned i, float d, float y) const {
 #pragma unroll
         for (int k = 0; k < V; ++k) {
-            const std::size_t c = first + static_cast<std::size_t>(k) * stride, j0 = 4 * c;
+            const unsigned c = first + static_cast<unsigned>(k) * stride, j0 = 4 * c;
             if (c >= T4) continue;
             float pv[4] = {0.f, 0.f, 0.f, 0.f};
             if ((full >> k) & 1u) {
@@ -143,10 +144,10 @@ causal_softmax_block(SoftmaxArgs a) {
     extern __shared__ __align__(16) float staged[];  // EXACT: T floats
     load_exp2_table(tab);
     __syncthreads();
-    const std::size_t T4 = a.T / 4;
+    const unsigned T4 = static_cast<unsigned>(a.T / 4);
     for (std::size_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
-        const std::size_t i = row % a.T;
-        const std::size_t begin = i + 1 > a.window ? i + 1 - a.window : 0;
+        const unsigned i = static_cast<unsigned>(row % a.T);
+        const unsigned begin = i + 1 > a.window ? static_cast<unsigned>(i + 1 - a.window) : 0u;
         const float4* src = reinterpret_cast<const float4*>(a.scores + row * a.ld);
         float4* dst = reinterpret_cast<float4*>(a.probs + row * a.ld);
         RowPart<V, EXACT> part;
@@ -196,11 +197,11 @@ causal_softmax_warp(SoftmaxArgs a) {
     __syncthreads();
     const unsigned lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* mine = staged + static_cast<std::size_t>(warp) * a.T;
-    const std::size_t T4 = a.T / 4;
+    const unsigned T4 = static_cast<unsigned>(a.T / 4);
     for (std::size_t row = static_cast<std::size_t>(blockIdx.x) * kWarpRowWarps + warp; row < a.rows;
          row += static_cast<std::size_t>(gridDim.x) * kWarpRowWarps) {
-        const std::size_t i = row % a.T;
-        const std::size_t begin = i + 1 > a.window ? i + 1 - a.window : 0;
+        const unsigned i = static_cast<unsigned>(row % a.T);
+        const unsigned begin = i + 1 > a.window ? static_cast<unsigned>(i + 1 - a.window) : 0u;
         const float4* src = reinterpret_cast<const float4*>(a.scores + row * a.ld);
         float4* dst = reinterpret_cast<float4*>(a.probs + row * a.ld);
         RowPart<V, EXACT> part;
