@@ -474,9 +474,11 @@ struct BlockAttention {
         // ---- out[r][h][d] = sum_w p[w][r * 4 + h] v[w][d], ascending w ----
         // Threads 0..127: rows ra = 2 * (tid / 64) and ra + 1, dimensions
         // 2 * (tid % 64) and + 1, all four heads: 16 chains per thread, each
-        // value pair read once for both rows. The deeper row's window is the
-        // shallower one's shifted by at most one key at each end, so each
-        // tile splits into (shallower only) (both) (deeper only) key runs.
+        // value pair read once for both rows, run as 8 packed pairs (heads
+        // 2j and 2j + 1 in the two lanes of one fma.rn.f32x2, each lane its
+        // own chain). The deeper row's window is the shallower one's shifted
+        // by at most one key at each end, so each tile splits into
+        // (shallower only) (both) (deeper only) key runs.
         const bool pv = tid < 128;
         const int ra = 2 * static_cast<int>(tid >> 6), dp = static_cast<int>(tid & 63);
         constexpr int kNone = 1 << 30;
@@ -491,7 +493,9 @@ struct BlockAttention {
             lob = static_cast<int>((pr + 1 > a.window ? pr + 1 - a.window : 0) - begin);
             hib = static_cast<int>(pr - begin);
         }
-        float acc[2][kGroup][2] = {};
+        unsigned long long acc[2][2][2];  // [row][head pair][d]: heads (2j, 2j + 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) (&acc[0][0][0])[i] = 0ull;
         issue_values(0, wg);  // the key buffers were released by the last QK barrier
         for (int t = 0; t < tiles; ++t) {
             if (t + 1 < tiles) issue_values(t + 1, wg);
@@ -502,37 +506,33 @@ struct BlockAttention {
                 const int w0a = max(loa - tb, 0), w1a = min(hia - tb, kBlkKeys - 1);
                 const int w0b = lob == kNone ? kNone : max(lob - tb, 0), w1b = min(hib - tb, kBlkKeys - 1);
                 const float* prow = scores + static_cast<std::size_t>(tb) * kCombos + 4 * ra;
+                // one key for row r: p = (heads 0,1 | heads 2,3), v = (d0, d1)
+                auto step = [&](int r, const ulonglong2 p, const unsigned long long vx, const unsigned long long vy) {
+                    acc[r][0][0] = f2_fma(p.x, vx, acc[r][0][0]);
+                    acc[r][0][1] = f2_fma(p.x, vy, acc[r][0][1]);
+                    acc[r][1][0] = f2_fma(p.y, vx, acc[r][1][0]);
+                    acc[r][1][1] = f2_fma(p.y, vy, acc[r][1][1]);
+                };
                 const int e1 = min(w1a, w0b - 1);
                 for (int w = w0a; w <= e1; ++w) {  // shallower row only
-                    const float4 pa = *reinterpret_cast<const float4*>(prow + w * kCombos);
+                    const ulonglong2 pa = *reinterpret_cast<const ulonglong2*>(prow + w * kCombos);
                     const float2 vv = *reinterpret_cast<const float2*>(buf + w * kKeyPitch);
-                    acc[0][0][0] = __fmaf_rn(pa.x, vv.x, acc[0][0][0]); acc[0][0][1] = __fmaf_rn(pa.x, vv.y, acc[0][0][1]);
-                    acc[0][1][0] = __fmaf_rn(pa.y, vv.x, acc[0][1][0]); acc[0][1][1] = __fmaf_rn(pa.y, vv.y, acc[0][1][1]);
-                    acc[0][2][0] = __fmaf_rn(pa.z, vv.x, acc[0][2][0]); acc[0][2][1] = __fmaf_rn(pa.z, vv.y, acc[0][2][1]);
-                    acc[0][3][0] = __fmaf_rn(pa.w, vv.x, acc[0][3][0]); acc[0][3][1] = __fmaf_rn(pa.w, vv.y, acc[0][3][1]);
+                    step(0, pa, f2_pack(vv.x, vv.x), f2_pack(vv.y, vv.y));
                 }
                 const int e2 = min(w1a, w1b);
 #pragma unroll 8
                 for (int w = max(w0a, w0b); w <= e2; ++w) {  // both rows
-                    const float4 pa = *reinterpret_cast<const float4*>(prow + w * kCombos);
-                    const float4 pb = *reinterpret_cast<const float4*>(prow + w * kCombos + 4);
+                    const ulonglong2 pa = *reinterpret_cast<const ulonglong2*>(prow + w * kCombos);
+                    const ulonglong2 pb = *reinterpret_cast<const ulonglong2*>(prow + w * kCombos + 4);
                     const float2 vv = *reinterpret_cast<const float2*>(buf + w * kKeyPitch);
-                    acc[0][0][0] = __fmaf_rn(pa.x, vv.x, acc[0][0][0]); acc[0][0][1] = __fmaf_rn(pa.x, vv.y, acc[0][0][1]);
-                    acc[0][1][0] = __fmaf_rn(pa.y, vv.x, acc[0][1][0]); acc[0][1][1] = __fmaf_rn(pa.y, vv.y, acc[0][1][1]);
-                    acc[0][2][0] = __fmaf_rn(pa.z, vv.x, acc[0][2][0]); acc[0][2][1] = __fmaf_rn(pa.z, vv.y, acc[0][2][1]);
-                    acc[0][3][0] = __fmaf_rn(pa.w, vv.x, acc[0][3][0]); acc[0][3][1] = __fmaf_rn(pa.w, vv.y, acc[0][3][1]);
-                    acc[1][0][0] = __fmaf_rn(pb.x, vv.x, acc[1][0][0]); acc[1][0][1] = __fmaf_rn(pb.x, vv.y, acc[1][0][1]);
-                    acc[1][1][0] = __fmaf_rn(pb.y, vv.x, acc[1][1][0]); acc[1][1][1] = __fmaf_rn(pb.y, vv.y, acc[1][1][1]);
-                    acc[1][2][0] = __fmaf_rn(pb.z, vv.x, acc[1][2][0]); acc[1][2][1] = __fmaf_rn(pb.z, vv.y, acc[1][2][1]);
-                    acc[1][3][0] = __fmaf_rn(pb.w, vv.x, acc[1][3][0]); acc[1][3][1] = __fmaf_rn(pb.w, vv.y, acc[1][3][1]);
+                    const unsigned long long vx = f2_pack(vv.x, vv.x), vy = f2_pack(vv.y, vv.y);
+                    step(0, pa, vx, vy);
+                    step(1, pb, vx, vy);
                 }
                 for (int w = max(w1a + 1, w0b); w <= w1b; ++w) {  // deeper row only
-                    const float4 pb = *reinterpret_cast<const float4*>(prow + w * kCombos + 4);
+                    const ulonglong2 pb = *reinterpret_cast<const ulonglong2*>(prow + w * kCombos + 4);
                     const float2 vv = *reinterpret_cast<const float2*>(buf + w * kKeyPitch);
-                    acc[1][0][0] = __fmaf_rn(pb.x, vv.x, acc[1][0][0]); acc[1][0][1] = __fmaf_rn(pb.x, vv.y, acc[1][0][1]);
-                    acc[1][1][0] = __fmaf_rn(pb.y, vv.x, acc[1][1][0]); acc[1][1][1] = __fmaf_rn(pb.y, vv.y, acc[1][1][1]);
-                    acc[1][2][0] = __fmaf_rn(pb.z, vv.x, acc[1][2][0]); acc[1][2][1] = __fmaf_rn(pb.z, vv.y, acc[1][2][1]);
-                    acc[1][3][0] = __fmaf_rn(pb.w, vv.x, acc[1][3][0]); acc[1][3][1] = __fmaf_rn(pb.w, vv.y, acc[1][3][1]);
+                    step(1, pb, f2_pack(vv.x, vv.x), f2_pack(vv.y, vv.y));
                 }
             }
             __syncthreads();  // buffer t & 1 is refilled next
@@ -542,8 +542,11 @@ struct BlockAttention {
             if (pv && ra + rr < g) {
                 float* o = a.out + ((first + ra + rr) * a.q_heads + kh * kGroup) * 128 + 2 * dp;
 #pragma unroll
-                for (int h = 0; h < kGroup; ++h)
-                    *reinterpret_cast<float2*>(o + h * 128) = make_float2(acc[rr][h][0], acc[rr][h][1]);
+                for (int j = 0; j < 2; ++j) {
+                    const float2 d0 = f2_unpack(acc[rr][j][0]), d1 = f2_unpack(acc[rr][j][1]);  // (head 2j, 2j + 1)
+                    *reinterpret_cast<float2*>(o + (2 * j) * 128) = make_float2(d0.x, d1.x);
+                    *reinterpret_cast<float2*>(o + (2 * j + 1) * 128) = make_float2(d0.y, d1.y);
+                }
             }
         __syncthreads();  // scores / chain / tile are reused by the next group
         return true;
