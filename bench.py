@@ -39,7 +39,7 @@ METRIC = "non-GEMM prefill tokens/s (64x2048 prompts, 32 layers; layer-op HBM GB
 # DRAM bytes (read + write) per node row of a kernel launch, from one ncu
 # capture of that kernel on a smaller case of the same workload (8192 rows;
 # profiles/fused_combine_add_ln_config5.md), scaled to a launch by rows.
-TRAFFIC_BYTES_PER_ROW = {"fused": (402.787072e6 + 212.106752e6) / 8192}
+TRAFFIC_BYTES_PER_ROW = {"fused": (402.782208e6 + 212.583936e6) / 8192}
 
 
 def parse():
