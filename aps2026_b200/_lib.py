@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_moe_route": (C.c_int, [_vp, _sz, _sz, _f32, _f32] + [_vp] * 10 + [_sz, _vp]),
     "b2_moe_route_noalloc": (C.c_int, [_vp, _sz, _sz, _f32, _f32] + [_vp] * 9 + [_vp]),
     "b2_silu_mul": (C.c_int, [_vp, _sz, _vp, _sz, _vp, _sz, _sz, _sz, _vp]),
+    "b2_silu_mul_flags": (C.c_int, [_vp, _sz, _vp, _sz, _vp, _sz, _sz, _sz, _u32, _vp]),
     "b2_moe_combine": (C.c_int, [_vp, _sz, _vp, _vp, _vp, _sz, _sz, _vp]),
     "b2_add": (C.c_int, [_vp, _vp, _sz, _vp]),
     "b2_prefix_trie_build": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _sz, _vp]),

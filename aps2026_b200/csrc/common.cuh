@@ -40,8 +40,8 @@ __host__ __device__ inline bool aligned16(const void* p) {
 int sm_count();
 
 // Gated SiLU launch (moe.cu) with the exponential mode chosen by the caller:
-// b2_silu_mul passes exact = true (bit-exact always); b2_prefill_layers the
-// mode of its flags.
+// b2_silu_mul passes exact = true (bit-exact always); b2_silu_mul_flags and
+// b2_prefill_layers the mode of their flags.
 int silu_mul_launch(const float* gate, std::size_t ld_gate, const float* up, std::size_t ld_up, float* out,
                     std::size_t ld_out, std::size_t rows, std::size_t cols, bool exact, b2_stream_t stream);
 

@@ -533,6 +533,12 @@ int b2_silu_mul(const float* gate, size_t ld_gate, const float* up, size_t ld_up
     return b2::silu_mul_launch(gate, ld_gate, up, ld_up, out, ld_out, rows, cols, true, stream);
 }
 
+int b2_silu_mul_flags(const float* gate, size_t ld_gate, const float* up, size_t ld_up, float* out,
+                      size_t ld_out, size_t rows, size_t cols, uint32_t flags, b2_stream_t stream) {
+    return b2::silu_mul_launch(gate, ld_gate, up, ld_up, out, ld_out, rows, cols,
+                               (flags & B2_FLAG_EXACT_ORDER) != 0, stream);
+}
+
 int b2_moe_combine(const float* expert_out, size_t expert_rows, const uint8_t* routes,
                    const uint32_t* route_positions, float* out, size_t T, size_t h,
                    b2_stream_t stream) {

@@ -304,10 +304,11 @@ def moe_route_gpu(logits, out: MoeRouting | None = None, ws: RouteWorkspace | No
     return out
 
 
-def silu_mul_gpu(gate, up, out) -> None:
+def silu_mul_gpu(gate, up, out, exact: bool = True) -> None:
     """out = silu(gate) * up (tensor_ops::silu_mul_gpu, include/tensor.h:85).
     2-D views with a row stride (e.g. halves of a [2T, 896] gate|up buffer)
-    are accepted."""
+    are accepted. exact=True (the reference's contract) is bit-exact;
+    exact=False is the tree-order mode's expf form (b2_silu_mul_flags)."""
     if gate.shape != up.shape or out.shape != gate.shape:
         raise InvalidArgument("silu_mul shape")
     if gate.dim() == 1:
@@ -316,8 +317,13 @@ def silu_mul_gpu(gate, up, out) -> None:
         if t.dim() != 2 or t.stride(1) != 1 or not t.is_cuda or t.dtype != torch.float32:
             raise InvalidArgument("silu_mul layout")
     rows, cols = gate.shape
-    _check(_lib.lib().b2_silu_mul(gate.data_ptr(), gate.stride(0), up.data_ptr(), up.stride(0),
-                                  out.data_ptr(), out.stride(0), rows, cols, _stream()), "silu_mul_gpu")
+    if exact:
+        rc = _lib.lib().b2_silu_mul(gate.data_ptr(), gate.stride(0), up.data_ptr(), up.stride(0),
+                                    out.data_ptr(), out.stride(0), rows, cols, _stream())
+    else:
+        rc = _lib.lib().b2_silu_mul_flags(gate.data_ptr(), gate.stride(0), up.data_ptr(), up.stride(0),
+                                          out.data_ptr(), out.stride(0), rows, cols, 0, _stream())
+    _check(rc, "silu_mul_gpu")
 
 
 def moe_combine_gpu(expert_out, routes, route_positions, out) -> None:

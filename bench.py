@@ -407,7 +407,7 @@ def run_config(args) -> dict:
 
         def chain():
             ops.moe_route_gpu(logits, routing, ws)
-            ops.silu_mul_gpu(gu[:, :448], gu[:, 448:], act)
+            ops.silu_mul_gpu(gu[:, :448], gu[:, 448:], act, exact=args.exact)
             ops.moe_combine_gpu(eo, routing.routes, routing.route_positions, out)
         nbytes = (T * 16 * 4 + T * 2 + 2 * T * 4 * 2) + 2 * T * 448 * 12 + (2 * T * 4096 * 4 + T * 4096 * 4 + T * 10)
         work, tokens = "config 3: top-2 routing T=8192 + SiLU [16384, 2x448] + un-permute to [8192, 4096]", T

@@ -26,15 +26,15 @@
  *     message of the calling thread's last failure.
  *
  * Floating point: by default reductions (LayerNorm moments, softmax
- * denominators) are tree-shaped, the softmax (and, inside
- * b2_prefill_layers, the SiLU) exponentials are CUDA's expf and their
+ * denominators) are tree-shaped, the softmax and SiLU exponentials
+ * (b2_silu_mul_flags, and inside b2_prefill_layers) are CUDA's expf and their
  * quotients a multiplication by a rounded reciprocal, and results agree with
  * the reference kernels within 1e-5 relative OR 1e-6 absolute. With
  * B2_FLAG_EXACT_ORDER reductions run in the reference's serial ascending
  * order, exponentials are the reference's (float)exp((double)x) and
  * divisions correctly rounded, and results agree bit for bit. Functions
  * without a flags argument (b2_silu_mul, b2_rope, b2_moe_combine, b2_add)
- * are always bit-exact. Index/integer outputs (gather, routing,
+ * are always bit-exact; b2_silu_mul_flags is the SiLU with a mode. Index/integer outputs (gather, routing,
  * permutation) are always bit-exact.
  */
 #ifndef APS2026_B200_H
@@ -297,6 +297,17 @@ int b2_moe_route_noalloc(const float* logits, size_t T, size_t E,
 int b2_silu_mul(const float* gate, size_t ld_gate, const float* up,
                 size_t ld_up, float* out, size_t ld_out, size_t rows,
                 size_t cols, b2_stream_t stream);
+
+/*
+ * b2_silu_mul with the numerics mode of `flags`, like the other
+ * floating-point ops: B2_FLAG_EXACT_ORDER is b2_silu_mul (bit-exact); 0
+ * evaluates exp(-g) with CUDA's expf and the quotient with __fdividef
+ * (within 1e-5 relative OR 1e-6 absolute of the reference; no reference
+ * counterpart of its own).
+ */
+int b2_silu_mul_flags(const float* gate, size_t ld_gate, const float* up,
+                      size_t ld_up, float* out, size_t ld_out, size_t rows,
+                      size_t cols, uint32_t flags, b2_stream_t stream);
 
 /*
  * out[t, :] = 0.5 * expert_out[p_lo, :] + 0.5 * expert_out[p_hi, :], where

@@ -287,6 +287,23 @@ def test_silu_mul_bitexact(ops, cuda, rows, cols):
     oracle.assert_bitexact(to_host(out), oracle.silu_mul(gate, up), "silu_mul")
 
 
+@pytest.mark.parametrize("rows,cols", [(16384, 448), (5, 7), (3, 1000)])
+def test_silu_mul_tree_mode(ops, cuda, rows, cols):
+    """b2_silu_mul_flags without B2_FLAG_EXACT_ORDER: expf and __fdividef,
+    within the tree-order tolerance, including the saturated tails."""
+    import torch
+
+    g = rng(61)
+    gate = normal(g, (rows, cols), std=30.0)
+    gate.ravel()[:4] = np.float32([-200.0, 200.0, -88.5, 0.0])[: min(4, gate.size)]
+    up = normal(g, (rows, cols))
+    out = torch.empty((rows, cols), dtype=torch.float32, device=cuda)
+    gd, ud = to_dev(gate, cuda), to_dev(up, cuda)
+    ops.silu_mul_gpu(gd, ud, out, exact=False)
+    _sync()
+    oracle.assert_close(to_host(out), oracle.silu_mul(gate, up), what="silu_mul tree mode")
+
+
 def test_silu_mul_concatenated_layout(ops, cuda):
     import torch
 
