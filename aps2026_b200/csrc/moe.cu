@@ -388,7 +388,11 @@ silu_mul_scalar(const float* __restrict__ gate, std::size_t ldg, const float* __
 
 // ---- weighted un-permute ----------------------------------------------------
 
-constexpr int kRowThreads = 256;
+// One float4 of each expert row per thread, 1024 threads per row: measured
+// at 32,768 x 4096 as 6664 GB/s against 6342 for 256 threads x 4 float4 and
+// 6554 for 512 x 2.
+constexpr int kRowThreads = 1024;
+constexpr int kRowUnroll = 1;
 
 template <bool VEC>
 __global__ void __launch_bounds__(kRowThreads)
@@ -403,10 +407,10 @@ moe_combine_rows(const float* __restrict__ expert_out, std::size_t expert_rows,
             const std::size_t h4 = h / 4;
             const float4* e4 = reinterpret_cast<const float4*>(expert_out);
             float4* o4 = reinterpret_cast<float4*>(out) + t * h4;
-            for (std::size_t j0 = threadIdx.x; j0 < h4; j0 += kRowThreads * 4) {
-                float4 lo[4], hi[4];
+            for (std::size_t j0 = threadIdx.x; j0 < h4; j0 += kRowThreads * kRowUnroll) {
+                float4 lo[kRowUnroll], hi[kRowUnroll];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < kRowUnroll; ++k) {
                     const std::size_t j = j0 + static_cast<std::size_t>(k) * kRowThreads;
                     if (j < h4) {
                         lo[k] = cr.lo < expert_rows ? ld_stream(e4 + cr.lo * h4 + j) : zero4();
@@ -414,7 +418,7 @@ moe_combine_rows(const float* __restrict__ expert_out, std::size_t expert_rows,
                     }
                 }
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < kRowUnroll; ++k) {
                     const std::size_t j = j0 + static_cast<std::size_t>(k) * kRowThreads;
                     if (j < h4) st_plain(o4 + j, combine4(lo[k], hi[k]));
                 }
