@@ -5,18 +5,22 @@
 // ln_stage / ln_moments / ln_write (:2017-2128). There a whole 256-thread
 // CTA waits while thread 0 sums the row twice serially from shared memory.
 //
-// Here (default, tree order) the row lives in registers: 256 threads x V
-// float4 (V = 4 at h = 4096), loaded with 128-bit streaming loads, mean and
-// variance come from two register passes with warp shuffles and one shared
-// slot per warp, and the output is written straight from registers -- the
-// row crosses HBM exactly once in each direction. CTAs loop over rows
-// (grid = one resident wave of the device).
+// Here (default, tree order) the row lives in registers: THREADS x V float4
+// (at h = 4096: 256 x 4 for plain LN, 512 x 2 for the two- and three-input
+// forms), loaded with 128-bit streaming loads, mean and variance come from
+// two register passes with warp shuffles and one shared slot per warp, and
+// the output is written straight from registers -- the row crosses HBM
+// exactly once in each direction. CTAs loop over rows (grid = one resident
+// wave of the device). Rows too long for registers are staged in shared
+// memory by bulk (TMA) copies.
 //
-// With B2_FLAG_EXACT_ORDER the row is also staged to shared memory and one
-// thread forms both moments in ascending order exactly as ln_serial_sum /
-// ln_serial_var do (var += t * t as a fused multiply-add), so the output is
-// bit-identical to the reference; 128-thread CTAs keep more rows resident
-// per SM to overlap those serial chains.
+// With B2_FLAG_EXACT_ORDER the moments are formed in ascending order exactly
+// as ln_serial_sum / ln_serial_var do (var += t * t as a fused
+// multiply-add), so the output is bit-identical to the reference: for plain
+// LN over many rows by the 32-row batched kernel (one warp runs 32 rows'
+// chains side by side), otherwise by one thread per row over the row staged
+// in shared memory, with 128-thread CTAs keeping more rows resident per SM
+// to overlap those serial chains.
 //
 // Output: y = fma((x - mean) * inv, gamma, beta), inv = 1 / sqrtf(var / h +
 // eps), the reference's ln_write arithmetic (:2043-2047).
