@@ -60,7 +60,8 @@ def parse():
                    help="run a rank's chunks one after another on one stream (default: concurrent streams, "
                         "chunk 0 at the highest priority)")
     p.add_argument("--chunk-fractions", default="",
-                   help="comma-separated shares of a rank's tokens per sub-batch, in order (default: balanced)")
+                   help="comma-separated shares of a rank's tokens per sub-batch, in order (default with the "
+                        "default 3 chunks at N > 1: 0.5,0.375,0.125; otherwise balanced)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-kernel-timing", action="store_true",
                    help="no per-launch events in the timed region (diagnostic; the line then lacks kernels/roofline)")
@@ -182,6 +183,11 @@ def run_ours(args):
     tokens_total = sum(len(p) for p in prompts)
     chunks = args.chunks or (1 if world == 1 else 3)
     fractions = [float(f) for f in args.chunk_fractions.split(",")] if args.chunk_fractions else None
+    if fractions is None and world > 1 and chunks == 3:
+        # decreasing chunks: the last chunk's gather to rank 0 is the one left
+        # exposed, and 4:3:1 also computed faster than equal thirds on one
+        # rank's config-5 share (15.52 vs 15.70 ms for 16,384 rows)
+        fractions = [0.5, 0.375, 0.125]
     plan = chunk_plan(prompts, world, chunks, fractions)
     sizes = {tuple(sum(len(prompts[i]) for i in part) for part in parts) for parts in plan}
     if len(sizes) != 1:
@@ -328,9 +334,12 @@ def run_ours(args):
             "config": {"workload": f"config 5: {args.prompts} prompts x {args.length} tokens, {args.layers} layers, "
                                    "non-GEMM path, final hidden states gathered to rank 0",
                        "prompts": args.prompts, "tokens_per_prompt": args.length, "layers": args.layers,
-                       "node_rows_per_rank": rows, "chunks_per_rank": len(runner.pipes), "standin_pool": pool,
+                       "node_rows_per_rank": rows, "chunks_per_rank": len(runner.pipes),
+                       "chunk_tokens": [runner.batches[c].tokens for c in range(len(runner.pipes))],
+                       "standin_pool": pool,
                        "exact_order": args.exact,
-                       "l2": "inputs larger than L2 (every kernel streams >= 100 MB per launch)",
+                       "l2": "inputs larger than L2 (a step streams >= 90 GB per rank; the GEMM stand-in sets "
+                             "rotate by layer, so no launch re-reads another launch's inputs)",
                        "parallelism": f"prompt shards x{world}" + (", NCCL gather to rank 0 overlapped by chunk"
                                                                   if world > 1 else "")},
             "hbm_gbs_algorithmic": round(bpr["total"] * rows * world / (ms_per_step / 1e3) / 1e9, 1),
