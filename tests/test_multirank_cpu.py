@@ -129,13 +129,18 @@ def test_chunk_plan_fractions():
 
     prompts = [np.full(2048, i, dtype=np.int32) for i in range(64)]
     for fr, want in (((0.75, 0.25), [6, 2]), ((0.5, 0.5), [4, 4]), ((0.4, 0.35, 0.25), [3, 3, 2]),
-                     ((0.5, 0.3, 0.2), [4, 2, 2])):
+                     ((0.5, 0.3, 0.2), [4, 2, 2]), ((0.5, 0.375, 0.125), [4, 3, 1])):
         plan = chunk_plan(prompts, 8, len(fr), fr)
         for parts in plan:
             assert [len(p) for p in parts] == want
             flat = [i for p in parts for i in p]
             assert flat == sorted(flat)  # consecutive, in order
         assert sorted(i for parts in plan for p in parts for i in p) == list(range(64))
+    # bench.py's default shares at N > 1 give every rank the same chunk sizes
+    # at 2, 4 and 8 ranks (the per-chunk gather moves equal buffers)
+    for world, want in ((2, [16, 12, 4]), (4, [8, 6, 2]), (8, [4, 3, 1])):
+        plan = chunk_plan(prompts, world, 3, (0.5, 0.375, 0.125))
+        assert all([len(p) for p in parts] == want for parts in plan)
     # prompts sharing a first token stay in one chunk
     same = [np.array([7, 1, 2]), np.array([7, 1, 3]), np.array([9, 9]), np.array([5, 5])]
     plan = chunk_plan(same, 1, 2, (0.5, 0.5))
