@@ -22,6 +22,18 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) <= exported
 
 
+@pytest.mark.parametrize("cmd", [["gcc", "-std=c99", "-x", "c"], ["g++", "-std=c++17", "-x", "c++"]])
+def test_header_is_plain_c_and_cpp(cmd):
+    """The ABI header compiles warning-free as C99 (what a cgo / ctypes /
+    N-API binding includes) and as C++."""
+    from pathlib import Path
+
+    header = Path(__file__).resolve().parents[1] / "include" / "aps2026_b200.h"
+    r = subprocess.run(cmd + ["-Wall", "-Wextra", "-pedantic", "-Werror", "-fsyntax-only", str(header)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
 def test_binding_table_covers_header():
     assert set(_lib.declared_functions()) == set(_lib.SIGNATURES)
 
