@@ -98,3 +98,26 @@ def test_close_mask_or_criterion():
     want = np.array([1.0, 1e-3, 0.0, 1.0], np.float32)
     got = np.array([1.0 + 9e-6, 1e-3 + 9e-7, 9e-7, np.nan], np.float32)
     assert oracle.close_mask(got, want).tolist() == [True, True, True, False]
+
+
+def test_bytes_per_row_accounting():
+    """The algorithmic bytes behind every GB/s figure: each logical tensor
+    read or written once. The reference's unfused config-5 sequence moves
+    6,835,072 B per row (per layer: add + LN 65,536, RoPE 20,480, add + LN
+    65,536, routing 82, SiLU 10,752, un-permute 49,162; minus layer 0's carry
+    32,768; plus gather 32,768 and the final add + LN 65,536); the fused
+    un-permute + add + LN saves the 16 KB write and re-read of each MoE
+    output row per layer."""
+    from aps2026_b200 import prefill
+
+    h = 4096 * 4
+    d = prefill.bytes_per_row(32)
+    assert d["gather"] == 2 * h and d["ln0"] == 2 * h
+    assert d["rope"] == 2 * (16 + 4) * 128 * 4
+    assert d["add_ln"] == 4 * h
+    assert d["route"] == 16 * 4 + 2 + 2 * 4 * 2
+    assert d["silu"] == 2 * 448 * 12
+    assert d["fused"] == 49_162 + 4 * h - 2 * h  # un-permute + add + LN, one pass
+    reference = 32 * (65_536 + 20_480 + 65_536 + 82 + 10_752 + 49_162) - 32_768 + 32_768 + 65_536
+    assert reference == 6_835_072
+    assert d["total"] == reference - 32 * 2 * h == 5_786_496
