@@ -378,12 +378,72 @@ class HostStage:
         return prompts, lens, total, last
 
 
+def chunk_tokens(prompts: Sequence[np.ndarray], plan: list) -> list:
+    """tokens[r][c]: token rows of rank r's chunk c under `plan`
+    (shard.chunk_plan); every rank computes the same table."""
+    return [[sum(len(prompts[i]) for i in part) for part in parts] for parts in plan]
+
+
+class FinalGather:
+    """Collects every rank's final hidden states (token rows, chunk by chunk)
+    on rank 0 with point-to-point transfers: for chunk c each rank r > 0
+    sends its rows to rank 0 and rank 0 receives them into a buffer of
+    exactly that size, so ranks may hold different token counts and
+    different numbers of chunks (prompts of unequal length shard unevenly).
+
+    post(c, rows) issues chunk c's transfers as one batch
+    (torch.distributed.batch_isend_irecv: a grouped ncclSend / ncclRecv on
+    NCCL's stream, which first waits for the stream current at the call, so
+    a chunk is sent once its rows are written). Every rank calls post for
+    every c < chunks(), in order, including chunks it does not hold itself
+    (rank 0 receives them). Transfers between two ranks are matched in
+    posting order. Rank 0's own rows stay where they are."""
+
+    def __init__(self, tokens: list, rank: int, hidden: int, device, dtype=None, group=None):
+        import torch.distributed as dist
+
+        self.dist, self.tokens, self.rank, self.group = dist, tokens, rank, group
+        self.world = len(tokens)
+        dtype = dtype or torch.float32
+        self.recv = {}
+        if rank == 0:
+            for r in range(1, self.world):
+                for c, n in enumerate(tokens[r]):
+                    self.recv[(c, r)] = torch.empty((n, hidden), device=device, dtype=dtype)
+
+    def chunks(self) -> int:
+        return max(len(t) for t in self.tokens)
+
+    def _peer(self, r: int) -> int:
+        """Global rank of group rank r."""
+        return r if self.group is None else self.dist.get_global_rank(self.group, r)
+
+    def post(self, c: int, rows: "torch.Tensor | None") -> list:
+        d = self.dist
+        ops = []
+        if self.rank == 0:
+            for r in range(1, self.world):
+                if c < len(self.tokens[r]):
+                    ops.append(d.P2POp(d.irecv, self.recv[(c, r)], self._peer(r), self.group))
+        elif c < len(self.tokens[self.rank]):
+            if rows is None or rows.shape[0] != self.tokens[self.rank][c]:
+                raise ValueError(f"FinalGather: chunk {c} of rank {self.rank} has the wrong row count")
+            ops.append(d.P2POp(d.isend, rows, self._peer(0), self.group))
+        return d.batch_isend_irecv(ops) if ops else []
+
+    def rows(self, c: int, r: int, own: "torch.Tensor | None" = None) -> "torch.Tensor":
+        """Rank 0, after the transfers completed: rank r's chunk c (`own` is
+        rank 0's own rows for r == 0)."""
+        return own if r == 0 else self.recv[(c, r)]
+
+
 class ShardedPrefill:
     """One rank's share of a prompt batch on one GPU, split into `chunks`
     sub-batches. Each chunk runs all layers (b2_prefill_layers), writes its
-    final hidden states as token rows, and -- with world > 1 -- is gathered
-    to rank 0 by NCCL on the collective's own stream while the next chunk
-    computes, so only the last chunk's gather is exposed.
+    final hidden states as token rows, and -- with world > 1 -- is sent to
+    rank 0 (FinalGather: NCCL send / recv on the collective's own stream)
+    while the next chunk computes, so only the last chunk's transfer is
+    exposed. Ranks may hold different token counts.
 
     With `concurrent` (default) the chunks run on their own streams, chunk 0
     at the highest priority: its launches take the SMs first, and the later
@@ -395,8 +455,7 @@ class ShardedPrefill:
                  standins: Sequence[StandIns], layers: int, rank: int = 0, exact: bool = False, group=None,
                  concurrent: bool = True, device_trie: bool = True):
         """`plan` is shard.chunk_plan(prompts, world, chunks): this rank runs
-        plan[rank]; every rank's chunk c must have the same token count (the
-        per-chunk gather moves equal-sized buffers)."""
+        plan[rank]; chunk sizes may differ between ranks."""
         self.device, self.world, self.rank, self.group = device, len(plan), rank, group
         world = self.world
         self.layers = layers
@@ -416,9 +475,9 @@ class ShardedPrefill:
             r0 += b.rows
         self.rows = r0
         self.tokens = sum(b.tokens for b in self.batches)
-        self.recv = None
-        if world > 1 and rank == 0:
-            self.recv = [[torch.empty_like(t) for _ in range(world)] for t in self.send]
+        self.gather = None
+        if world > 1:
+            self.gather = FinalGather(chunk_tokens(prompts, plan), rank, HIDDEN, device, group=group)
         self._stage = HostStage(device, self.batches, on_device=device_trie)
         self._last_idx = None
         self.streams = None
@@ -434,11 +493,9 @@ class ShardedPrefill:
         return sum(launches_per_run(self.layers) + (0 if d else 1) for d in self.direct)
 
     def step(self, timers=None) -> None:
-        """Enqueues the whole share (+ the gathers) after the work already on
-        the current stream; on return the current stream is ordered after
-        every chunk and every gather."""
-        import torch.distributed as dist
-
+        """Enqueues the whole share (+ the transfers to rank 0) after the work
+        already on the current stream; on return the current stream is
+        ordered after every chunk and every transfer."""
         cur = torch.cuda.current_stream(self.device)
         works = []
         for c, pipe in enumerate(self.pipes):
@@ -451,9 +508,11 @@ class ShardedPrefill:
                 else:
                     pipe.run(stream=s, timer=timers[c] if timers else None)
                     pipe.expand_to_tokens(self.send[c])
-                if self.world > 1:  # the collective's stream waits for s
-                    works.append(dist.gather(self.send[c], self.recv[c] if self.rank == 0 else None, dst=0,
-                                             group=self.group, async_op=True))
+                if self.gather is not None:  # NCCL's stream waits for s
+                    works += self.gather.post(c, self.send[c])
+        if self.gather is not None:  # chunks other ranks hold beyond this rank's own
+            for c in range(len(self.pipes), self.gather.chunks()):
+                works += self.gather.post(c, None)
         if self.streams:
             for s in self.streams:
                 cur.wait_stream(s)
@@ -483,15 +542,21 @@ class ShardedPrefill:
         (asynchronous: the row indices were uploaded once)."""
         if self._last_idx is None:
             self._last_idx = []
-            for c in range(len(self.batches)):
+            for c in range(max(len(p) for p in self.plan)):
                 for r in range(self.world):
+                    if c >= len(self.plan[r]):
+                        continue
                     ends = np.cumsum([len(self.all_prompts[i]) for i in self.plan[r][c]]) - 1
                     self._last_idx.append((c, r, torch.from_numpy(ends.astype(np.int32)).to(self.device)))
         k = 0
         for c, r, idx in self._last_idx:
-            src = self.recv[c][r] if self.recv is not None else self.send[c]
+            src = self.send[c] if r == 0 else self.gather.rows(c, r)
             ops.gather_rows_gpu(src, idx, out[k:k + idx.numel()])
             k += idx.numel()
+
+    def release(self) -> None:
+        """Drops the receive buffers (before the process group is destroyed)."""
+        self.gather = None
 
 
 class StageTimer:

@@ -6,20 +6,25 @@
 // src/tensor.cu (add_inplace_gpu, silu_mul_gpu, layer_norm_gpu,
 // add_layer_norm_gpu, apply_rope_gpu, apply_rope_tree_gpu, attention_gpu,
 // attention_tree_gpu, both gather_rows_gpu overloads). src/layer.cu,
-// src/model.cu and src/main.cpp
-// compile unchanged: same signatures, same Tensor handling (inputs through
-// cuda_data(), outputs through cuda_data_write(), the legacy default
-// stream), and the same exception types with the reference's messages
-// (std::invalid_argument on a shape mismatch, std::runtime_error on a CUDA
-// failure). The routing and un-permute inside moe_forward_grouped_gpu are
-// replaced in place (see the b2 calls its body makes in the integration
-// notes), because that function also launches the reference's GEMMs.
+// src/model.cu and src/main.cpp compile unchanged: same signatures, same
+// Tensor handling (inputs through cuda_data(), outputs through
+// cuda_data_write(), the legacy default stream), and the same exception
+// types (std::invalid_argument on a shape mismatch, std::runtime_error on a
+// CUDA failure).
+//
+// moe_forward_grouped_gpu keeps its place in src/tensor.cu (it launches the
+// reference's private expert GEMMs); its routing and un-permute call the
+// two hooks of moe_hook.h, defined at the end of this file, after the edit
+// that apply_moe_hook.py makes to its body.
 //
 // Reductions keep the reference's serial order (B2_FLAG_EXACT_ORDER) so the
 // drop-in reproduces the reference's outputs bit for bit, which its
 // end-to-end validation against answers.bin relies on (routing downstream of
 // a LayerNorm flips on a last-ulp change).
 #include <cstdint>
+#include <cstring>
+#include <map>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -28,12 +33,13 @@
 
 #include "aps2026_b200.h"
 #include "config.h"
+#include "moe_hook.h"
 #include "tensor.h"
 
-namespace tensor_ops {
 namespace {
 
 constexpr std::uint32_t kFlags = B2_FLAG_EXACT_ORDER;
+constexpr cudaStream_t kStream = nullptr;  // the reference runs everything on the legacy stream
 
 void check(int rc, const char* what) {
     if (rc == B2_OK) return;
@@ -42,137 +48,200 @@ void check(int rc, const char* what) {
     throw std::runtime_error(msg);
 }
 
-void cuda_check(cudaError_t e, const char* what) {
-    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+void cuda_ok(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string("aps2026_b200 shim, ") + what + ": " +
+                                                   cudaGetErrorString(e));
 }
 
-// Device RoPE table, built on the host by b2_rope_table and cached like the
-// reference's rope_table() static (src/tensor.cu:2695-2737).
-struct RopeTable {
-    float* cosine = nullptr;
-    float* sine = nullptr;
-    std::size_t max_seq = 0, half = 0;
-    float theta = 0.0f;
-};
-
-RopeTable& rope_table(std::size_t max_seq, std::size_t head_dim, float theta) {
-    static RopeTable t;
-    const std::size_t half = head_dim / 2;
-    if (t.cosine && t.max_seq >= max_seq && t.half == half && t.theta == theta) return t;
-    if (t.cosine) cudaFree(t.cosine);
-    if (t.sine) cudaFree(t.sine);
-    t = RopeTable{};
-    std::vector<float> c(max_seq * half), s(max_seq * half);
-    check(b2_rope_table(max_seq, head_dim, theta, c.data(), s.data()), "rope table");
-    cuda_check(cudaMalloc(&t.cosine, c.size() * sizeof(float)), "cudaMalloc rope cosine");
-    cuda_check(cudaMalloc(&t.sine, s.size() * sizeof(float)), "cudaMalloc rope sine");
-    cuda_check(cudaMemcpy(t.cosine, c.data(), c.size() * sizeof(float), cudaMemcpyHostToDevice),
-               "copy rope cosine");
-    cuda_check(cudaMemcpy(t.sine, s.data(), s.size() * sizeof(float), cudaMemcpyHostToDevice), "copy rope sine");
-    t.max_seq = max_seq;
-    t.half = half;
-    t.theta = theta;
-    return t;
+std::size_t grow_to(std::size_t need) {
+    std::size_t cap = 4096;
+    while (cap < need) cap <<= 1;
+    return cap;
 }
 
-// Per-segment positions of a packed batch, cached per seq_lens like the
-// reference's packed_meta() (src/tensor.cu:2662-2693).
-const std::uint32_t* packed_positions(const std::vector<std::size_t>& lens, std::size_t* rows,
-                                      std::size_t* max_seq) {
-    static std::vector<std::size_t> key;
-    static std::uint32_t* pos = nullptr;
-    static std::size_t n = 0, longest = 0;
-    if (pos && key == lens) {
-        *rows = n;
-        *max_seq = longest;
-        return pos;
-    }
-    std::vector<std::uint32_t> host;
-    longest = 0;
-    for (std::size_t len : lens) {
-        for (std::size_t p = 0; p < len; ++p) host.push_back(static_cast<std::uint32_t>(p));
-        if (len > longest) longest = len;
-    }
-    if (pos) cudaFree(pos);
-    pos = nullptr;
-    n = host.size();
-    if (n) {
-        cuda_check(cudaMalloc(&pos, n * sizeof(std::uint32_t)), "cudaMalloc packed positions");
-        cuda_check(cudaMemcpy(pos, host.data(), n * sizeof(std::uint32_t), cudaMemcpyHostToDevice),
-                   "copy packed positions");
-    }
-    key = lens;
-    *rows = n;
-    *max_seq = longest;
-    return pos;
-}
-
-// The packed-segment layout of attention_gpu in the compact chain form of
-// b2_attention_tree_compact: segment b's rows offsets[b] .. offsets[b + 1]
-// are their own chain, so row r's keys are rows offsets[seg[r]] .. + pos
-// (token_node = identity). Cached per seq_lens like packed_positions.
-struct SegmentChains {
-    std::uint32_t* seg = nullptr;       // [rows] segment of each row
-    std::uint32_t* offsets = nullptr;   // [segments + 1]
-    std::uint32_t* identity = nullptr;  // [rows]
-};
-
-const SegmentChains& segment_chains(const std::vector<std::size_t>& lens) {
-    static std::vector<std::size_t> key;
-    static SegmentChains c;
-    if (c.seg && key == lens) return c;
-    for (std::uint32_t* p : {c.seg, c.offsets, c.identity})
-        if (p) cudaFree(p);
-    c = SegmentChains{};
-    std::vector<std::uint32_t> seg, offsets{0}, identity;
-    for (std::size_t b = 0; b < lens.size(); ++b) {
-        for (std::size_t p = 0; p < lens[b]; ++p) {
-            seg.push_back(static_cast<std::uint32_t>(b));
-            identity.push_back(static_cast<std::uint32_t>(identity.size()));
+// ---- host -> device staging ---------------------------------------------------
+//
+// Everything the library needs in device memory that the reference's Tensor
+// API does not hand over as device memory -- RoPE tables, positions and
+// chains of packed segments, gather indices given as a host vector, the
+// routing workspace -- lives in a Stage: a grow-only device buffer filled
+// from a grow-only pinned host buffer by cudaMemcpyAsync on the legacy
+// stream, so each upload is ordered before the kernel that reads it without
+// synchronising the device. An event recorded after each upload guards the
+// pinned buffer before it is filled again. `key` records what the device
+// buffer holds, so an unchanged table is not uploaded twice.
+class Stage {
+public:
+    // Pinned host memory of at least `bytes`, free to overwrite.
+    void* host(std::size_t bytes) {
+        if (pending_) {
+            cuda_ok(cudaEventSynchronize(done_), "staging: wait for the previous upload");
+            pending_ = false;
         }
-        offsets.push_back(static_cast<std::uint32_t>(identity.size()));
+        if (bytes > host_bytes_) {
+            if (host_) cuda_ok(cudaFreeHost(host_), "staging: release pinned buffer");
+            host_bytes_ = grow_to(bytes);
+            cuda_ok(cudaMallocHost(&host_, host_bytes_), "staging: pinned buffer");
+        }
+        return host_;
     }
-    auto upload = [](const std::vector<std::uint32_t>& h, std::uint32_t** d, const char* what) {
-        if (h.empty()) return;
-        cuda_check(cudaMalloc(d, h.size() * sizeof(std::uint32_t)), what);
-        cuda_check(cudaMemcpy(*d, h.data(), h.size() * sizeof(std::uint32_t), cudaMemcpyHostToDevice), what);
-    };
-    upload(seg, &c.seg, "segment chains: rows");
-    upload(offsets, &c.offsets, "segment chains: offsets");
-    upload(identity, &c.identity, "segment chains: identity");
-    key = lens;
-    return c;
+
+    // Device memory of at least `bytes`; growing drops what it held.
+    void* device(std::size_t bytes) {
+        if (bytes > dev_bytes_) {
+            if (dev_) cuda_ok(cudaFree(dev_), "staging: release device buffer");
+            dev_bytes_ = grow_to(bytes);
+            cuda_ok(cudaMalloc(&dev_, dev_bytes_), "staging: device buffer");
+            key.clear();
+        }
+        return dev_;
+    }
+
+    // The first `bytes` of the host buffer into the device buffer.
+    void* upload(std::size_t bytes) {
+        void* d = device(bytes);
+        if (!done_) cuda_ok(cudaEventCreateWithFlags(&done_, cudaEventDisableTiming), "staging: event");
+        cuda_ok(cudaMemcpyAsync(d, host_, bytes, cudaMemcpyHostToDevice, kStream), "staging: upload");
+        cuda_ok(cudaEventRecord(done_, kStream), "staging: record upload");
+        pending_ = true;
+        return d;
+    }
+
+    std::vector<std::uint64_t> key;
+
+private:
+    void* host_ = nullptr;
+    void* dev_ = nullptr;
+    std::size_t host_bytes_ = 0, dev_bytes_ = 0;
+    cudaEvent_t done_ = nullptr;
+    bool pending_ = false;
+};
+
+// The stages of one device. The reference keeps one set of statics for the
+// whole process; keying by device keeps a multi-GPU host correct.
+struct DeviceStages {
+    Stage rope, segments, rows, route_ws;
+    std::size_t rope_rows = 0;  // table rows the rope stage holds
+};
+
+DeviceStages& stages() {
+    static std::mutex mu;
+    static std::map<int, DeviceStages> per_device;
+    int dev = 0;
+    cuda_ok(cudaGetDevice(&dev), "current device");
+    std::lock_guard<std::mutex> lock(mu);
+    return per_device[dev];
 }
 
-// Staging for the std::vector gather overload (the reference's
-// device_rows(), src/tensor.cu:2739-2753).
-const std::uint32_t* device_rows(const std::vector<std::size_t>& rows) {
-    static std::uint32_t* ptr = nullptr;
-    static std::size_t capacity = 0;
-    if (capacity < rows.size()) {
-        if (ptr) cudaFree(ptr);
-        cuda_check(cudaMalloc(&ptr, rows.size() * sizeof(std::uint32_t)), "cudaMalloc row indices");
-        capacity = rows.size();
+std::uint64_t bits_of(float f) {
+    std::uint32_t u;
+    std::memcpy(&u, &f, sizeof u);
+    return u;
+}
+
+// cos | sin tables of b2_rope_table in one device buffer, covering at least
+// max_seq positions (rounded up to a power of two, so a growing batch does
+// not rebuild the table each time).
+struct RopeTables {
+    const float* cos;
+    const float* sin;
+    std::size_t rows;
+};
+
+RopeTables rope_tables(std::size_t max_seq, std::size_t head_dim, float theta) {
+    DeviceStages& st = stages();
+    Stage& s = st.rope;
+    const std::size_t half = head_dim / 2;
+    const bool same_kind = s.key.size() == 2 && s.key[0] == head_dim && s.key[1] == bits_of(theta);
+    if (!same_kind || st.rope_rows < max_seq) {
+        std::size_t rows = 1;
+        while (rows < max_seq) rows <<= 1;
+        const std::size_t n = rows * half;
+        float* h = static_cast<float*>(s.host(2 * n * sizeof(float)));
+        check(b2_rope_table(rows, head_dim, theta, h, h + n), "rope table");
+        s.upload(2 * n * sizeof(float));
+        s.key = {head_dim, bits_of(theta)};
+        st.rope_rows = rows;
     }
-    std::vector<std::uint32_t> compact(rows.begin(), rows.end());
-    cuda_check(cudaMemcpy(ptr, compact.data(), compact.size() * sizeof(std::uint32_t), cudaMemcpyHostToDevice),
-               "copy row indices");
-    return ptr;
+    const float* d = static_cast<const float*>(s.device(0));
+    return {d, d + st.rope_rows * half, st.rope_rows};
+}
+
+// Device index arrays of a packed segment batch (the layout attention_gpu and
+// apply_rope_gpu take: segment b's rows follow segment b - 1's):
+//   pos      [rows]          position of the row in its segment
+//   seg      [rows]          segment of the row
+//   identity [rows]          r -> r (rows are their own chain entries)
+//   offsets  [segments + 1]  first row of each segment
+// Uploaded once per distinct seq_lens.
+struct Segments {
+    const std::uint32_t* pos;
+    const std::uint32_t* seg;
+    const std::uint32_t* identity;
+    const std::uint32_t* offsets;
+    std::size_t rows, max_seq;
+};
+
+Segments segments(const std::vector<std::size_t>& lens) {
+    Stage& s = stages().segments;
+    std::size_t rows = 0, longest = 0;
+    for (std::size_t n : lens) {
+        rows += n;
+        longest = n > longest ? n : longest;
+    }
+    std::vector<std::uint64_t> key(lens.begin(), lens.end());
+    key.push_back(~std::uint64_t{0});  // an empty key never matches
+    const std::size_t words = 3 * rows + lens.size() + 1;
+    if (s.key != key) {
+        auto* h = static_cast<std::uint32_t*>(s.host(words * sizeof(std::uint32_t)));
+        std::uint32_t* pos = h;
+        std::uint32_t* seg = h + rows;
+        std::uint32_t* id = h + 2 * rows;
+        std::uint32_t* off = h + 3 * rows;
+        std::size_t r = 0;
+        for (std::size_t b = 0; b < lens.size(); ++b) {
+            off[b] = static_cast<std::uint32_t>(r);
+            for (std::size_t p = 0; p < lens[b]; ++p, ++r) {
+                pos[r] = static_cast<std::uint32_t>(p);
+                seg[r] = static_cast<std::uint32_t>(b);
+                id[r] = static_cast<std::uint32_t>(r);
+            }
+        }
+        off[lens.size()] = static_cast<std::uint32_t>(r);
+        s.upload(words * sizeof(std::uint32_t));
+        s.key = std::move(key);
+    }
+    const auto* d = static_cast<const std::uint32_t*>(s.device(0));
+    return {d, d + rows, d + 2 * rows, d + 3 * rows, rows, longest};
+}
+
+// The host row list of the std::vector gather overload as device uint32.
+const std::uint32_t* staged_rows(const std::vector<std::size_t>& rows) {
+    Stage& s = stages().rows;
+    auto* h = static_cast<std::uint32_t*>(s.host(rows.size() * sizeof(std::uint32_t)));
+    for (std::size_t i = 0; i < rows.size(); ++i) {
+        if (rows[i] > UINT32_MAX) throw std::invalid_argument("gather_rows_gpu: row index beyond 32 bits");
+        h[i] = static_cast<std::uint32_t>(rows[i]);
+    }
+    s.key.clear();
+    return static_cast<const std::uint32_t*>(s.upload(rows.size() * sizeof(std::uint32_t)));
 }
 
 }  // namespace
 
+namespace tensor_ops {
+
 void add_inplace_gpu(Tensor& a, const Tensor& b) {
     if (a.size() != b.size()) throw std::invalid_argument("add shape");
     a.cuda_data();
-    check(b2_add(a.cuda_data_write(), b.cuda_data(), a.size(), nullptr), "k_add launch");
+    check(b2_add(a.cuda_data_write(), b.cuda_data(), a.size(), kStream), "add_inplace_gpu");
 }
 
 void silu_mul_gpu(const Tensor& gate, const Tensor& up, Tensor& out) {
     if (gate.size() != up.size() || out.size() != gate.size()) throw std::invalid_argument("silu_mul shape");
     const std::size_t n = gate.size();
-    check(b2_silu_mul(gate.cuda_data(), n, up.cuda_data(), n, out.cuda_data_write(), n, 1, n, nullptr),
-          "k_silu_mul launch");
+    check(b2_silu_mul(gate.cuda_data(), n, up.cuda_data(), n, out.cuda_data_write(), n, 1, n, kStream),
+          "silu_mul_gpu");
 }
 
 void layer_norm_gpu(const Tensor& x, const Tensor& weight, const Tensor& bias, float eps, Tensor& y) {
@@ -181,8 +250,8 @@ void layer_norm_gpu(const Tensor& x, const Tensor& weight, const Tensor& bias, f
     if (weight.size() != h || bias.size() != h || y.size() != x.size())
         throw std::invalid_argument("layer norm shape");
     check(b2_layer_norm(x.cuda_data(), weight.cuda_data(), bias.cuda_data(), y.cuda_data_write(), rows, h, eps,
-                        kFlags, nullptr),
-          "k_layer_norm launch");
+                        kFlags, kStream),
+          "layer_norm_gpu");
 }
 
 void add_layer_norm_gpu(Tensor& x, const Tensor& residual, const Tensor& weight, const Tensor& bias, float eps,
@@ -193,31 +262,30 @@ void add_layer_norm_gpu(Tensor& x, const Tensor& residual, const Tensor& weight,
         throw std::invalid_argument("add layer norm shape");
     x.cuda_data();
     check(b2_add_layer_norm(x.cuda_data_write(), residual.cuda_data(), weight.cuda_data(), bias.cuda_data(),
-                            y.cuda_data_write(), rows, h, eps, kFlags, nullptr),
-          "k_add_layer_norm launch");
+                            y.cuda_data_write(), rows, h, eps, kFlags, kStream),
+          "add_layer_norm_gpu");
 }
 
 void apply_rope_gpu(Tensor& q, Tensor& k, const std::vector<std::size_t>& seq_lens, std::size_t q_heads,
                     std::size_t kv_heads, std::size_t head_dim, float theta) {
-    std::size_t rows = 0, max_seq = 0;
-    const std::uint32_t* pos = packed_positions(seq_lens, &rows, &max_seq);
-    RopeTable& t = rope_table(max_seq, head_dim, theta);
+    const Segments sg = segments(seq_lens);
+    const RopeTables t = rope_tables(sg.max_seq, head_dim, theta);
     q.cuda_data();
     k.cuda_data();
-    check(b2_rope(q.cuda_data_write(), k.cuda_data_write(), pos, rows, q_heads, kv_heads, head_dim, t.cosine,
-                  t.sine, t.max_seq, nullptr),
-          "k_rope launch");
+    check(b2_rope(q.cuda_data_write(), k.cuda_data_write(), sg.pos, sg.rows, q_heads, kv_heads, head_dim, t.cos,
+                  t.sin, t.rows, kStream),
+          "apply_rope_gpu");
 }
 
 void apply_rope_tree_gpu(Tensor& q, Tensor& k, const std::uint32_t* row_pos, std::size_t rows,
                          std::size_t max_seq, std::size_t q_heads, std::size_t kv_heads, std::size_t head_dim,
                          float theta) {
-    RopeTable& t = rope_table(max_seq, head_dim, theta);
+    const RopeTables t = rope_tables(max_seq, head_dim, theta);
     q.cuda_data();
     k.cuda_data();
-    check(b2_rope(q.cuda_data_write(), k.cuda_data_write(), row_pos, rows, q_heads, kv_heads, head_dim, t.cosine,
-                  t.sine, t.max_seq, nullptr),
-          "k_rope(tree) launch");
+    check(b2_rope(q.cuda_data_write(), k.cuda_data_write(), row_pos, rows, q_heads, kv_heads, head_dim, t.cos,
+                  t.sin, t.rows, kStream),
+          "apply_rope_tree_gpu");
 }
 
 // GQA-4 (the model's layout) runs the prefix-tree kernel over segment chains,
@@ -228,14 +296,12 @@ void attention_gpu(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& ou
                    std::size_t head_dim) {
     if (q_heads != 4 * kv_heads)
         throw std::invalid_argument("attention_gpu: only GQA-4 is implemented by the B200 library");
-    std::size_t rows = 0, max_seq = 0;
-    const std::uint32_t* pos = packed_positions(seq_lens, &rows, &max_seq);
-    if (rows == 0) return;
-    const SegmentChains& c = segment_chains(seq_lens);
-    check(b2_attention_tree_compact(q.cuda_data(), k.cuda_data(), v.cuda_data(), out.cuda_data_write(), pos, c.seg,
-                                    c.offsets, seq_lens.size(), c.identity, rows, max_seq, rows, q_heads, kv_heads,
-                                    head_dim, apss26::SLIDING_WINDOW, kFlags, nullptr),
-          "k_attention_grouped_gqa4 launch");
+    const Segments sg = segments(seq_lens);
+    if (sg.rows == 0) return;
+    check(b2_attention_tree_compact(q.cuda_data(), k.cuda_data(), v.cuda_data(), out.cuda_data_write(), sg.pos,
+                                    sg.seg, sg.offsets, seq_lens.size(), sg.identity, sg.rows, sg.max_seq, sg.rows,
+                                    q_heads, kv_heads, head_dim, apss26::SLIDING_WINDOW, kFlags, kStream),
+          "attention_gpu");
 }
 
 void attention_tree_gpu(const Tensor& q, const Tensor& k, const Tensor& v, Tensor& out,
@@ -244,22 +310,45 @@ void attention_tree_gpu(const Tensor& q, const Tensor& k, const Tensor& v, Tenso
                         std::size_t head_dim) {
     (void)max_seq;  // positions are bounded by anc_stride
     check(b2_attention_tree(q.cuda_data(), k.cuda_data(), v.cuda_data(), out.cuda_data_write(), row_pos, anc,
-                            anc_stride, rows, q_heads, kv_heads, head_dim, apss26::SLIDING_WINDOW, kFlags, nullptr),
-          "k_attention_tree_gqa4 launch");
+                            anc_stride, rows, q_heads, kv_heads, head_dim, apss26::SLIDING_WINDOW, kFlags, kStream),
+          "attention_tree_gpu");
 }
 
 void gather_rows_gpu(const Tensor& x, const std::vector<std::size_t>& rows, Tensor& out) {
     const std::size_t h = x.size(x.ndim() - 1);
-    check(b2_gather_rows(x.cuda_data(), x.size() / h, h, device_rows(rows), rows.size(), out.cuda_data_write(),
-                         nullptr),
-          "k_gather_rows launch");
+    if (rows.empty()) return;
+    check(b2_gather_rows(x.cuda_data(), x.size() / h, h, staged_rows(rows), rows.size(), out.cuda_data_write(),
+                         kStream),
+          "gather_rows_gpu");
 }
 
 void gather_rows_gpu(const Tensor& x, const RowIndexBuffer& rows, Tensor& out) {
     if (rows.empty()) return;
     const std::size_t h = x.size(x.ndim() - 1);
-    check(b2_gather_rows(x.cuda_data(), x.size() / h, h, rows.data(), rows.size(), out.cuda_data_write(), nullptr),
-          "k_gather_rows(dev) launch");
+    check(b2_gather_rows(x.cuda_data(), x.size() / h, h, rows.data(), rows.size(), out.cuda_data_write(), kStream),
+          "gather_rows_gpu (device rows)");
 }
 
 }  // namespace tensor_ops
+
+namespace b2_dropin {
+
+void moe_route(const float* router_logits, std::size_t rows, std::uint8_t* routes, std::uint32_t* counts,
+               std::uint32_t* offsets, std::uint32_t* assignment_rows, std::uint32_t* route_positions,
+               std::uint32_t* work_expert64, std::uint32_t* work_start64, std::uint32_t* work_expert128,
+               std::uint32_t* work_start128) {
+    std::size_t need = 0;
+    check(b2_moe_route_workspace_size(rows, apss26::NUM_EXPERTS, &need), "moe routing workspace");
+    void* ws = stages().route_ws.device(need);
+    check(b2_moe_route(router_logits, rows, apss26::NUM_EXPERTS, apss26::ROUTER_SCORE_QUANTUM, apss26::ROUTER_TIE_EPS,
+                       routes, counts, offsets, assignment_rows, route_positions, work_expert64, work_start64,
+                       work_expert128, work_start128, ws, need, kStream),
+          "moe routing");
+}
+
+void moe_combine(const float* expert_out, std::size_t expert_rows, const std::uint8_t* routes,
+                 const std::uint32_t* route_positions, float* out, std::size_t rows, std::size_t h) {
+    check(b2_moe_combine(expert_out, expert_rows, routes, route_positions, out, rows, h, kStream), "moe combine");
+}
+
+}  // namespace b2_dropin

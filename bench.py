@@ -37,8 +37,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "non-GEMM prefill tokens/s (64x2048 prompts, 32 layers; layer-op HBM GB/s in roofline)"
 # DRAM bytes (read + write) per node row of a kernel launch, from one ncu
-# capture of that kernel on a smaller case of the same workload (8192 rows;
-# profiles/fused_combine_add_ln_config5.md), scaled to a launch by rows.
+# capture of that kernel on a smaller case of the same workload (8192 rows),
+# scaled to a launch by rows.
 TRAFFIC_BYTES_PER_ROW = {"fused": (402.782208e6 + 212.583936e6) / 8192}
 
 
@@ -67,6 +67,9 @@ def parse():
                    help="no per-launch events in the timed region (diagnostic; the line then lacks kernels/roofline)")
     p.add_argument("--config", type=int, default=5, choices=[1, 2, 3, 4, 5],
                    help="BASELINE config; 5 (default) is the headline, 1-4 single-GPU op chains")
+    p.add_argument("--kernel", choices=KERNELS, default=None,
+                   help="time one launch kind alone on --rows rows (the ncu small case)")
+    p.add_argument("--rows", type=int, default=16384, help="--kernel: trie rows")
     return p.parse_args()
 
 
@@ -189,9 +192,6 @@ def run_ours(args):
         # rank's config-5 share (15.52 vs 15.70 ms for 16,384 rows)
         fractions = [0.5, 0.375, 0.125]
     plan = chunk_plan(prompts, world, chunks, fractions)
-    sizes = {tuple(sum(len(prompts[i]) for i in part) for part in parts) for parts in plan}
-    if len(sizes) != 1:
-        raise SystemExit("unequal shards: the per-chunk gather expects equal token counts on every rank")
 
     weights = Weights.make(dev, seed=4, layers=args.layers)
     rows = ShardedPrefill.rows_needed(prompts, plan[rank])
@@ -359,7 +359,7 @@ def run_ours(args):
             "standin_gen_s": round(t_gen, 2),
         }
     if dist:
-        runner.recv = None
+        runner.release()
         dist.barrier()
         dist.destroy_process_group()
     return result
@@ -529,6 +529,93 @@ def run_config(args) -> dict:
     return res
 
 
+# ---- one kernel on its own ---------------------------------------------------------------------
+
+KERNELS = ("ln", "add_ln", "fused", "rope", "silu", "combine", "gather", "route")
+
+
+def run_kernel(args) -> dict:
+    """One launch kind of the path alone on `--rows` trie rows at the
+    config.h shapes (hidden 4096, 16 / 4 heads of 128, 16 experts,
+    intermediate 448): L2 flushed (256 MB written) before each timed launch,
+    CUDA events around the launch on its stream, median over `--steps`.
+    Value: algorithmic GB/s (each tensor read or written once). This is the
+    small case the ncu summaries are captured on."""
+    import torch
+
+    from aps2026_b200 import ops, prefill as P
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    R, H = args.rows, P.HIDDEN
+    gen = torch.Generator(device=dev).manual_seed(11)
+    rn = lambda *s, std=1.0, mean=0.0: P._randn(s, gen, dev, mean, std)  # noqa: E731
+    emp = lambda *s: torch.empty(s, device=dev)  # noqa: E731
+    gamma, beta = rn(H, mean=1.0, std=0.1), rn(H, std=0.1)
+    flush = torch.empty(64 << 20, device=dev)
+    kind, exact = args.kernel, args.exact
+    if kind in ("fused", "combine"):
+        routing = ops.moe_route_gpu(rn(R, P.EXPERTS))
+    if kind == "ln":
+        x, y = rn(R, H), emp(R, H)
+        fn = lambda: ops.layer_norm_gpu(x, gamma, beta, 1e-5, y, exact=exact)  # noqa: E731
+        nbytes = 2 * R * H * 4 + 2 * H * 4
+    elif kind == "add_ln":
+        x, res, y = rn(R, H), rn(R, H), emp(R, H)
+        fn = lambda: ops.add_layer_norm_gpu(x, res, gamma, beta, 1e-5, y, exact=exact)  # noqa: E731
+        nbytes = 4 * R * H * 4 + 2 * H * 4
+    elif kind == "fused":
+        eo, carry, xo, y = rn(2 * R, H), rn(R, H), emp(R, H), emp(R, H)
+        fn = lambda: ops.moe_combine_add_layer_norm_gpu(eo, routing.routes, routing.route_positions, carry,  # noqa
+                                                        gamma, beta, 1e-5, xo, y, exact=exact)
+        nbytes = P.bytes_per_row(1)["fused"] * R + 2 * H * 4
+    elif kind == "rope":
+        q, k = rn(R, P.Q_HEADS * P.HEAD_DIM), rn(R, P.KV_HEADS * P.HEAD_DIM)
+        pos = (torch.arange(R, dtype=torch.int32, device=dev) % 2048).contiguous()
+        fn = lambda: ops.apply_rope_tree_gpu(q, k, pos, R, 2048, P.Q_HEADS, P.KV_HEADS, P.HEAD_DIM, 1e4)  # noqa
+        nbytes = P.bytes_per_row(1)["rope"] * R
+    elif kind == "silu":
+        gu, act = rn(2 * R, 2 * P.INTER), emp(2 * R, P.INTER)
+        fn = lambda: ops.silu_mul_gpu(gu[:, :P.INTER], gu[:, P.INTER:], act, exact=exact)  # noqa: E731
+        nbytes = P.bytes_per_row(1)["silu"] * R
+    elif kind == "combine":
+        eo, out = rn(2 * R, H), emp(R, H)
+        fn = lambda: ops.moe_combine_gpu(eo, routing.routes, routing.route_positions, out)  # noqa: E731
+        nbytes = 3 * R * H * 4 + R * (2 + 8)
+    elif kind == "gather":
+        emb, out = rn(P.VOCAB, H, std=0.02), emp(R, H)
+        ids = torch.randint(0, P.VOCAB, (R,), generator=gen, device=dev, dtype=torch.int32)
+        fn = lambda: ops.gather_rows_gpu(emb, ids, out)  # noqa: E731
+        nbytes = 2 * R * H * 4 + 4 * R
+    else:  # route
+        logits = rn(R, P.EXPERTS)
+        rt, ws = ops.alloc_routing(R, P.EXPERTS, dev), ops.RouteWorkspace(R, P.EXPERTS, dev)
+        fn = lambda: ops.moe_route_gpu(logits, rt, ws)  # noqa: E731
+        nbytes = P.bytes_per_row(1)["route"] * R
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(0) as clocks:
+        for a, b_ in ev:
+            flush.zero_()
+            a.record()
+            fn()
+            b_.record()
+        torch.cuda.synchronize()
+    ms = statistics.median(a.elapsed_time(b_) for a, b_ in ev)
+    peak, peak_kind = peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"metric": f"kernel {kind} algorithmic HBM GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": {"workload": f"{kind} on {R} rows (hidden {H})", "rows": R, "algorithmic_bytes": nbytes,
+                       "exact_order": exact, "l2": "flushed (256 MB written) before every timed launch"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 3), "peak_kind": peak_kind, "traffic": None},
+            "clocks": {k: v for k, v in clocks.summary().items() if k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+
+
 # ---- CPU baseline / reference arm ---------------------------------------------------------
 
 
@@ -563,7 +650,7 @@ def cpu_baseline_port(rows: int = 8192, budget_s: float = 10.0) -> dict:
         t += time.perf_counter() - t0
         passes += 1
     return {"value": round(rows * passes / 32 / t, 1), "unit": "tokens/s", "cores": oracle.num_threads(),
-            "kind": "port",
+            "cpu_model": cpu_model(), "kind": "port",
             "sample": f"oracle pipeline, {passes} one-layer passes over {rows} rows (gather + layer + final LN), "
                       f"{t:.1f} s, scaled to 32 layers"}
 
@@ -619,6 +706,86 @@ def reference_layer(rows: int, s, ln, emb, node_token, node_depth, lens) -> floa
     return total
 
 
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def reference_gpu_kernels(rows: int, layers: int, steps: int) -> dict:
+    """The reference's own non-GEMM kernels (src/tensor.cu, compiled from its
+    source into oracle/_ref/libref.so) on this GPU, for comparison with ours
+    on the same hardware: one decoder layer's sequence as forward_carry
+    launches it (k_add_layer_norm for the carried add + input LayerNorm,
+    k_rope on Q then K, k_add_layer_norm after attention, the routing
+    kernels, k_silu_mul, k_moe_combine) on `rows` rows with seeded stand-ins,
+    timed per kernel with CUDA events (median of `steps`), scaled to
+    `layers` layers plus the embedding gather and the final add + LN."""
+    import ctypes as C
+
+    import torch
+
+    import oracle
+    from aps2026_b200 import ops, prefill as P
+
+    r = oracle.ref()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(12)
+    rn = lambda *s, std=1.0, mean=0.0: P._randn(s, gen, dev, mean, std)  # noqa: E731
+    emp = lambda *s, dt=torch.float32: torch.empty(s, device=dev, dtype=dt)  # noqa: E731
+    H, s = P.HIDDEN, torch.cuda.current_stream().cuda_stream
+    x, carry, y = rn(rows, H), rn(rows, H), emp(rows, H)
+    w, b = rn(H, mean=1.0, std=0.1), rn(H, std=0.1)
+    q, k = rn(rows, P.Q_HEADS * P.HEAD_DIM), rn(rows, P.KV_HEADS * P.HEAD_DIM)
+    pos = (torch.arange(rows, dtype=torch.int32, device=dev) % 2048).contiguous()
+    cos, sin = ops.rope_table_gpu(2048, P.HEAD_DIM, 1e4, dev)
+    logits = rn(rows, P.EXPERTS)
+    n64, n128 = ops.queue_lengths(rows, P.EXPERTS)
+    rt = [emp(2 * rows, dt=torch.uint8), emp(P.EXPERTS, dt=torch.int32), emp(P.EXPERTS + 1, dt=torch.int32),
+          emp(2 * rows, dt=torch.int32), emp(2 * rows, dt=torch.int32), emp(n64, dt=torch.int32),
+          emp(n64, dt=torch.int32), emp(n128, dt=torch.int32), emp(n128, dt=torch.int32)]
+    gate, up, act = rn(2 * rows, P.INTER), rn(2 * rows, P.INTER), emp(2 * rows, P.INTER)
+    eo, out = rn(2 * rows, H), emp(rows, H)
+    emb = rn(P.VOCAB, H, std=0.02)
+    ids = torch.randint(0, P.VOCAB, (rows,), generator=gen, device=dev, dtype=torch.int32)
+    flush = torch.empty(64 << 20, device=dev)
+    pp = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    launch = {
+        "add_ln": lambda: r.ref_k_add_layer_norm(pp(x), pp(carry), pp(w), pp(b), pp(y), rows, H, 1e-5, s),
+        "rope": lambda: r.ref_k_rope(pp(q), pp(k), pp(pos), pp(cos), pp(sin), rows, P.Q_HEADS, P.KV_HEADS,
+                                     P.HEAD_DIM, s),
+        "route": lambda: r.ref_k_moe_route(pp(logits), rows, *[pp(t) for t in rt], s),
+        "silu": lambda: r.ref_k_silu_mul(pp(gate), pp(up), pp(act), 2 * rows * P.INTER, s),
+        "combine": lambda: r.ref_k_moe_combine(pp(eo), pp(rt[0]), pp(rt[4]), pp(out), rows, H, s),
+        "gather": lambda: r.ref_k_gather_rows(pp(emb), pp(ids), pp(out), rows, H, s),
+    }
+    ms = {}
+    for name, fn in launch.items():
+        if fn() != 0:
+            raise RuntimeError(f"reference kernel {name} failed to launch")
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a, e in ev:
+            flush.zero_()
+            a.record()
+            fn()
+            e.record()
+        torch.cuda.synchronize()
+        ms[name] = statistics.median(a.elapsed_time(e) for a, e in ev)
+    layer = 2 * ms["add_ln"] + ms["rope"] + ms["route"] + ms["silu"] + ms["combine"]
+    step = layers * layer + ms["gather"] + ms["add_ln"]
+    return {"value": round(rows / (step * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(step, 3),
+            "layer_ms": {k: round(v, 4) for k, v in ms.items()}, "rows": rows,
+            "what": f"the reference's own kernels (oracle/_ref/libref.so, src/tensor.cu built for sm_100a) on "
+                    f"{torch.cuda.get_device_name(dev)}: one layer on {rows} rows timed per kernel (median of "
+                    f"{steps}, L2 flushed), x {layers} layers + gather + final add-LN; k_silu_mul stands for the "
+                    f"SiLU epilogue the reference fuses into its expert GEMM"}
+
+
 def run_reference(args):
     import oracle
 
@@ -630,6 +797,9 @@ def run_reference(args):
         return {"impl": "reference", "unavailable": "oracle/_ref/libref.so (the reference built from its source) "
                                                     "is missing; build it with `make -C oracle` where the "
                                                     "reference tree exists"}
+    # One step of this arm = one bounded sample of the workload: one decoder
+    # layer's non-GEMM path over `rows` rows on the host cores. value scales
+    # its rate to the whole workload (layers x tokens), flagged extrapolated.
     rows = 2048
     prompts, emb, s, ln = cpu_sample_inputs(rows, seed=8)
     trie = oracle.prefix_trie(prompts, with_ancestors=False)
@@ -644,19 +814,30 @@ def run_reference(args):
                                     trie["node_depth"], lens))
     t_layer = statistics.mean(secs)
     tokens_total = args.prompts * args.length
-    ms_per_step = t_layer * args.layers * (tokens_total / rows) * 1e3
-    value = tokens_total / (ms_per_step / 1e3)
-    sample = (f"reference host ops (oracle/_ref) for LN / RoPE / add / SiLU*mul, oracle port for routing and "
-              f"un-permute; one layer on {rows} rows ({t_layer:.3f} s), scaled to {args.layers} layers x "
+    scale = args.layers * tokens_total / rows
+    value = tokens_total / (t_layer * scale)
+    sample = (f"one step = one decoder layer's non-GEMM path on {rows} rows: reference host ops (oracle/_ref) for "
+              f"LN / RoPE / add / SiLU*mul, oracle port for routing and un-permute (the reference's are private "
+              f"to PhiMoE); {t_layer:.3f} s per step, value scaled x{scale:g} to {args.layers} layers x "
               f"{tokens_total} tokens")
-    return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": f"config 5: {args.prompts} prompts x {args.length} tokens, "
-                                                        f"{args.layers} layers, non-GEMM path (CPU sample)"},
-            "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": oracle.num_threads(),
-                             "kind": "reference", "sample": sample},
-            "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    res = {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_layer * 1e3, 3),
+           "step_is": f"a bounded sample: one layer on {rows} rows", "extrapolated": True,
+           "scale_to_workload": scale,
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic", "config": {"workload": f"config 5: {args.prompts} prompts x {args.length} tokens, "
+                                                       f"{args.layers} layers, non-GEMM path (CPU sample)"},
+           "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": oracle.num_threads(),
+                            "cpu_model": cpu_model(), "kind": "reference", "sample": sample},
+           "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            res["reference_gpu_kernels"] = reference_gpu_kernels(args.prompts * args.length, args.layers, 5)
+    except Exception as exc:  # informational only; the arm's value is the CPU path
+        res["reference_gpu_kernels"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+    return res
 
 
 def main():
@@ -665,6 +846,9 @@ def main():
         res = run_reference(args)
         if res is not None:
             print(json.dumps(res))
+        return
+    if args.kernel:
+        print(json.dumps(run_kernel(args)))
         return
     if args.config != 5:
         print(json.dumps(run_config(args)))

@@ -9,10 +9,14 @@ this checks parity with the reference, not the course's answers.bin.
 PhiTinyMoEModel::generate exercises the trie path (gather_rows_gpu,
 layer_norm_gpu / add_layer_norm_gpu, apply_rope_tree_gpu,
 attention_tree_gpu); forward(use_gpu = true) the packed path
-(apply_rope_gpu, attention_gpu, add_inplace_gpu). The GEMMs, the MoE
-routing and the combine are the reference's in both libraries. Routing
-after every LayerNorm makes this a sharp test: a last-ulp difference in one
-LayerNorm output can flip an expert choice and change the logits.
+(apply_rope_gpu, attention_gpu, add_inplace_gpu). Both run every layer's
+MoE through moe_forward_grouped_gpu, whose routing (b2_moe_route) and
+un-permute (b2_moe_combine) the b2 library takes over through the hooks of
+aps2026_b200/shim/apply_moe_hook.py; the GEMMs are the reference's in both
+libraries. Routing after every LayerNorm makes this a sharp test: a
+last-ulp difference in one LayerNorm output, or one differently ordered
+assignment row, flips an expert choice or a GEMM row and changes the
+logits.
 """
 import os
 import subprocess

@@ -1,7 +1,10 @@
 """Prompt-sharded prefill on 2 GPUs (NCCL): every rank runs its chunks with
-b2_prefill_layers and the final hidden states are gathered to rank 0; the
-gathered rows equal a single-GPU run of the whole batch, bit for bit
-(B2_FLAG_EXACT_ORDER). Skipped with fewer than 2 GPUs."""
+b2_prefill_layers and the final hidden states are sent to rank 0
+(prefill.FinalGather: NCCL send / recv per chunk); the collected rows equal
+a single-GPU run of the whole batch, bit for bit (B2_FLAG_EXACT_ORDER).
+Cases: equal shards; prompts of ragged lengths (ranks and chunks of
+different token counts); and ranks holding different numbers of chunks.
+Skipped with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -55,7 +58,20 @@ def _standins_for(prompts, chunks, device, layers_pool):
     return sets
 
 
-def _run(rank, world, port, out_path):
+def _prompts(case):
+    from aps2026_b200 import prefill
+
+    if case == "equal":
+        return prefill.prompts_config5(seed=31, batch=8, length=96)
+    g = np.random.default_rng(32)
+    if case == "ragged":
+        return [g.integers(0, prefill.VOCAB, int(n)).astype(np.int32) for n in g.integers(40, 160, 9)]
+    # "uneven_chunks": rank 0 holds one chunk, rank 1 two (rank 0 receives a
+    # chunk index it has no rows of its own for)
+    return [g.integers(0, prefill.VOCAB, n).astype(np.int32) for n in (120, 100, 70)]
+
+
+def _run(rank, world, port, out_path, case):
     import torch
     import torch.distributed as dist
 
@@ -71,7 +87,7 @@ def _run(rank, world, port, out_path):
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                                 device_id=dev)
     try:
-        prompts = prefill.prompts_config5(seed=31, batch=8, length=96)
+        prompts = _prompts(case)
         plan = chunk_plan(prompts, world, 2)
         w = prefill.Weights.make(dev, 7, layers=HID_LAYERS)
         sets = _standins_for(prompts, plan[rank], dev, 2)
@@ -83,27 +99,31 @@ def _run(rank, world, port, out_path):
             torch.cuda.synchronize()
             np.save(out_path, last.cpu().numpy())
         if world > 1:
-            runner.recv = None
+            runner.release()
             dist.barrier()
     finally:
         if world > 1:
             dist.destroy_process_group()
 
 
-def test_two_gpu_gather_matches_one_gpu(tmp_path):
+@pytest.mark.parametrize("case", ["equal", "ragged", "uneven_chunks"])
+def test_two_gpu_gather_matches_one_gpu(tmp_path, case):
     import torch
     import torch.multiprocessing as mp
 
-    from aps2026_b200 import prefill
     from aps2026_b200.shard import chunk_plan, gather_order
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    prompts = _prompts(case)
+    plan = chunk_plan(prompts, 2, 2)
+    tokens = [[sum(len(prompts[i]) for i in part) for part in parts] for parts in plan]
+    if case != "equal":  # the case really is uneven
+        assert tokens[0] != tokens[1]
     two, one = str(tmp_path / "two.npy"), str(tmp_path / "one.npy")
-    mp.start_processes(_run, args=(2, _free_port(), two), nprocs=2, join=True, start_method="spawn")
-    mp.start_processes(_run, args=(1, _free_port(), one), nprocs=1, join=True, start_method="spawn")
-    prompts = prefill.prompts_config5(seed=31, batch=8, length=96)
-    o2 = gather_order(chunk_plan(prompts, 2, 2))
+    mp.start_processes(_run, args=(2, _free_port(), two, case), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_run, args=(1, _free_port(), one, case), nprocs=1, join=True, start_method="spawn")
+    o2 = gather_order(plan)
     o1 = gather_order(chunk_plan(prompts, 1, 2))
     got, want = np.load(two), np.load(one)
     pos1 = {p: k for k, p in enumerate(o1)}

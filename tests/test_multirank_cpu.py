@@ -3,9 +3,12 @@ trie per chunk, per-rank layer pipelines and the gather of final hidden
 states to rank 0 reproduce the single-process result row for row.
 
 Each rank runs the CPU oracle's layer pipeline on its chunks (the GPU ranks
-run b2_prefill_layers with the same plan) and rank 0 collects the chunks with
-torch.distributed.gather in shard.gather_order; the GEMM stand-ins are a
-fixed function of (prompt, position), so sharding cannot change any row.
+run b2_prefill_layers with the same plan) and rank 0 collects the chunks
+through prefill.FinalGather -- the point-to-point transfer the GPU ranks use,
+here over gloo -- in shard.gather_order; the GEMM stand-ins are a fixed
+function of (prompt, position), so sharding cannot change any row. Prompt
+sets with ragged lengths give ranks and chunks of different token counts
+and ranks with different numbers of chunks.
 """
 import os
 import socket
@@ -17,8 +20,12 @@ import torch.multiprocessing as mp
 HID, QH, KVH, HD, INTER, LAYERS = 32, 2, 1, 8, 16, 2
 
 
-def _prompts():
+def _prompts(case="equal"):
     g = np.random.default_rng(40)
+    if case == "ragged":  # unequal shards and chunks
+        return [g.integers(0, 500, int(n)).astype(np.int32) for n in g.integers(3, 20, 9)]
+    if case == "uneven_chunks":  # rank 0 holds one chunk, rank 1 two
+        return [g.integers(0, 500, n).astype(np.int32) for n in (12, 10, 7)]
     ps = [g.integers(0, 500, int(g.integers(8, 14))).astype(np.int32) for _ in range(8)]
     for i in range(1, 8, 2):  # pairs of prompts of equal length keep the rank shards equal in tokens
         ps[i] = g.integers(0, 500, len(ps[i - 1])).astype(np.int32)
@@ -67,23 +74,30 @@ def _run_chunk(prompts, idx):
     return y[trie["token_node"]]
 
 
-def _rank_main(rank, world, port, out_path):
+def _rank_main(rank, world, port, out_path, case):
     import torch
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        from aps2026_b200.prefill import FinalGather, chunk_tokens
         from aps2026_b200.shard import chunk_plan
 
-        prompts = _prompts()
+        prompts = _prompts(case)
         plan = chunk_plan(prompts, world, 2)
-        for c, idx in enumerate(plan[rank]):
-            send = torch.from_numpy(_run_chunk(prompts, idx))
-            recv = [torch.empty_like(send) for _ in range(world)] if rank == 0 else None
-            dist.gather(send, recv, dst=0)
-            if rank == 0:
-                np.save(f"{out_path}.{c}.npy", torch.cat(recv).numpy())
+        gather = FinalGather(chunk_tokens(prompts, plan), rank, HID, "cpu")
+        own, works = [], []
+        for c in range(gather.chunks()):
+            rows = torch.from_numpy(_run_chunk(prompts, plan[rank][c])) if c < len(plan[rank]) else None
+            own.append(rows)
+            works += gather.post(c, rows)
+        for w in works:
+            w.wait()
+        if rank == 0:
+            parts = [gather.rows(c, r, own[c]) for c in range(gather.chunks()) for r in range(world)
+                     if c < len(plan[r])]
+            np.save(out_path, torch.cat(parts).numpy())
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -110,17 +124,24 @@ def test_chunk_plan_covers_every_prompt_once():
     assert any({0, 1} <= set(s) for s in shards)
 
 
-def test_two_cpu_ranks_gather_matches_single_process(tmp_path):
+@pytest.mark.parametrize("case", ["equal", "ragged", "uneven_chunks"])
+def test_two_cpu_ranks_gather_matches_single_process(tmp_path, case):
+    from aps2026_b200.prefill import chunk_tokens
     from aps2026_b200.shard import chunk_plan, gather_order
 
     world = 2
-    out = str(tmp_path / "gathered")
-    mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world, join=True, start_method="spawn")
-    prompts = _prompts()
+    prompts = _prompts(case)
     plan = chunk_plan(prompts, world, 2)
-    got = np.concatenate([np.load(f"{out}.{c}.npy") for c in range(len(plan[0]))])
-    order = gather_order(plan)
-    want = np.concatenate([_run_chunk(prompts, [i]) for i in order])
+    tokens = chunk_tokens(prompts, plan)
+    if case == "ragged":
+        assert tokens[0] != tokens[1]
+    if case == "uneven_chunks":
+        assert len(plan[0]) != len(plan[1])
+    out = str(tmp_path / "gathered.npy")
+    mp.start_processes(_rank_main, args=(world, _free_port(), out, case), nprocs=world, join=True,
+                       start_method="spawn")
+    got = np.load(out)
+    want = np.concatenate([_run_chunk(prompts, [i]) for i in gather_order(plan)])
     np.testing.assert_array_equal(got, want)
 
 
@@ -137,7 +158,7 @@ def test_chunk_plan_fractions():
             assert flat == sorted(flat)  # consecutive, in order
         assert sorted(i for parts in plan for p in parts for i in p) == list(range(64))
     # bench.py's default shares at N > 1 give every rank the same chunk sizes
-    # at 2, 4 and 8 ranks (the per-chunk gather moves equal buffers)
+    # at 2, 4 and 8 ranks
     for world, want in ((2, [16, 12, 4]), (4, [8, 6, 2]), (8, [4, 3, 1])):
         plan = chunk_plan(prompts, world, 3, (0.5, 0.375, 0.125))
         assert all([len(p) for p in parts] == want for parts in plan)
@@ -150,23 +171,25 @@ def test_chunk_plan_fractions():
 
 
 def _rank_with_failed_peer(rank, world, port, out_path):
-    """Rank 1 'fails' (exits without cleanup) before its gather; rank 0's
-    gather must end with an error, not wait forever."""
+    """Rank 1 'fails' (exits without cleanup) before it sends its rows; rank
+    0's receive (FinalGather, as the GPU ranks use it) must end with an
+    error, not wait forever."""
     import datetime
     import time
 
-    import torch
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
     if rank == 1:
         os._exit(0)
+    from aps2026_b200.prefill import FinalGather
+
     t0 = time.monotonic()
-    send = torch.zeros(4, 8)
-    recv = [torch.empty_like(send) for _ in range(world)]
+    gather = FinalGather([[4], [4]], 0, 8, "cpu")
     try:
-        dist.gather(send, recv, dst=0)
+        for w in gather.post(0, None):
+            w.wait()
         status = "no error"
     except Exception as e:  # noqa: BLE001 -- any error type counts as detection
         status = "error " + type(e).__name__
