@@ -16,11 +16,11 @@
 //
 // With B2_FLAG_EXACT_ORDER the moments are formed in ascending order exactly
 // as ln_serial_sum / ln_serial_var do (var += t * t as a fused
-// multiply-add), so the output is bit-identical to the reference: for plain
-// LN over many rows by the 32-row batched kernel (one warp runs 32 rows'
-// chains side by side), otherwise by one thread per row over the row staged
-// in shared memory, with 128-thread CTAs keeping more rows resident per SM
-// to overlap those serial chains.
+// multiply-add), so the output is bit-identical to the reference: over many
+// rows by the chain pipeline (ln_exact_pipe: warps whose lanes run 16 rows'
+// chains side by side, fed by a ring of staged chunks), otherwise by one
+// thread per row over the row staged in shared memory, with 128-thread CTAs
+// keeping more rows resident per SM to overlap those serial chains.
 //
 // Output: y = fma((x - mean) * inv, gamma, beta), inv = 1 / sqrtf(var / h +
 // eps), the reference's ln_write arithmetic (:2043-2047).
@@ -344,125 +344,446 @@ ln_rows_bulk(LnArgs a) {
     }
 }
 
-// Reference-order (B2_FLAG_EXACT_ORDER) LayerNorm of many rows (plain
-// LayerNorm; the fused-add forms keep the per-row kernel, which measured
-// faster with their second and third input streams). The serial sums are 2h
-// dependent additions per row; issued one row per thread they leave 31 of a
-// warp's lanes idle. Here a CTA takes 32 rows at a time and warp 0 runs the
-// 32 rows' chains side by side, lane r summing row r's staged chunk in
-// ascending order, while the other 15 warps stage the next chunk
-// (kExactChunk floats of each row) into the other shared buffer with
-// coalesced 128-bit loads, 8 in flight per thread. Pass A forms the sums,
-// pass B the squared deviations (re-reading the 32 rows, which one CTA per
-// SM keeps within L2), pass C writes y with every thread. Same operations in
-// the same order as serial_moments, so the output is bit-identical to the
-// reference.
-constexpr int kExactRows = 32;
-constexpr int kExactChunk = 512;
-constexpr int kExactPitch = kExactChunk + 4;  // floats; spreads the lanes' rows over the banks
-constexpr int kExactThreads = 512;
+// ---- reference-order LayerNorm of many rows: the chain pipeline ----------------
+//
+// B2_FLAG_EXACT_ORDER forms the mean and the variance as the reference does
+// (ln_serial_sum / ln_serial_var, src/tensor.cu:2063-2128): one ascending
+// chain of h dependent additions per row for each, about 17 us of FP32
+// latency per row at h = 4096. Over many rows that latency has to overlap
+// the HBM traffic, so rows go through a pipeline, one CTA per SM, in
+// batches of 16 rows and "ticks" of one 128-float chunk of each row:
+//
+//   compute warps   stage, a ring of shared-memory stages ahead (8 stages
+//                   for plain LN, 5 with the residual, 4 with the
+//                   un-permute, as many as fit), the pass-A inputs of batch
+//                   b (x; x and the residual; or the carry and the two
+//                   expert rows), the pass-B tile of batch b - 1 and the
+//                   y-pass tile of batch b - 2 with gamma and beta, by
+//                   cp.async (16 bytes a thread; completion tracked by the
+//                   stage's mbarrier, so no copy holds registers); in the
+//                   add modes they form the row values of batch b (x + res,
+//                   or combine + carry), write them to x_out and into a tile
+//                   for chain A; and they write y of batch b - 2 from its
+//                   tile and the stats chain B published;
+//   chain warp A    lane r adds row r of batch b in ascending order -> mean;
+//   chain warp B    lane r accumulates (x - mean)^2 of row r of batch b - 1
+//                   as a fused multiply-add, ascending -> 1/sqrt(var/h+eps).
+//
+// The chains take 128 x 4 cycles a tick, less than a tick's HBM time. The
+// row values are read once from HBM and twice more (pass B, y), with L2
+// priorities that keep them resident for those re-reads. A thread stages,
+// reads back and re-reads only its own rows' float4 column, so its writes
+// of x_out order its later copies of them. Every wait is bounded; a wait
+// that gives up sets a shared abort flag that stops every role, and each
+// thread waits for its own copies before the CTA exits. Same operations in
+// the same order as serial_moments, so y is bit-identical to the reference.
+constexpr int kPipeRows = 16;
+constexpr int kPipeChunk = 128;                // floats of a row per tick
+constexpr int kPipePitch = kPipeChunk + 4;     // 528 B: lanes' rows start on distinct banks
+constexpr int kPipeTile = kPipeRows * kPipePitch;
+constexpr int kPipeMaxStages = 8;
+constexpr int kPipeComputeWarps = 8;
+constexpr int kPipeThreads = 32 * (2 + kPipeComputeWarps);
 
-__global__ void __launch_bounds__(kExactThreads, 1)
-ln_exact_batch(LnArgs a) {
+template <int MODE>
+constexpr int pipe_inputs() {
+    return MODE == kLN ? 1 : (MODE == kAddLN ? 2 : 3);
+}
+
+// Stages of the ring (as many as fit in shared memory; each holds a tick's
+// pass-A inputs, pass-B tile, y-pass tile and gamma / beta chunk).
+template <int MODE>
+constexpr int pipe_stages() {
+    return MODE == kLN ? 8 : (MODE == kAddLN ? 5 : 4);
+}
+
+// floats of one stage: NIN pass-A tiles, the pass-B tile, the y-pass tile,
+// and gamma | beta of the chunk
+template <int MODE>
+constexpr int pipe_stage_floats() {
+    return (pipe_inputs<MODE>() + 2) * kPipeTile + 2 * kPipeChunk;
+}
+
+// Dynamic shared memory: the stages, then (add modes) two tiles of row
+// values for chain A.
+template <int MODE>
+constexpr std::size_t pipe_smem() {
+    return (static_cast<std::size_t>(pipe_stages<MODE>()) * pipe_stage_floats<MODE>() +
+            (MODE == kLN ? 0 : 2) * kPipeTile) * sizeof(float);
+}
+
+struct PipeShared {
+    std::uint64_t full[kPipeMaxStages], empty[kPipeMaxStages];
+    std::uint64_t sfull[2], sempty[2];  // compute -> chain A: row-value tiles
+    std::uint64_t mfull[2], mempty[2];  // chain A -> chain B: means
+    std::uint64_t ifull[2], iempty[2];  // chain B -> compute: mean and 1/std
+    float mean_a[2][kPipeRows];
+    float mean_o[2][kPipeRows], inv_o[2][kPipeRows];
+    int abort;
+};
+
+__device__ __forceinline__ bool mbar_try(std::uint64_t* bar, unsigned parity) {
+    unsigned done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Gives up (and stops every role) after kMbarWaitNs of the global timer.
+__device__ __forceinline__ bool pipe_stop(volatile int* abort_flag, unsigned long long t0) {
+    if (*abort_flag) return true;
+    if (global_ns() - t0 > kMbarWaitNs) {
+        *abort_flag = 1;
+        flag_check(B2_CHECK_WAIT);
+        return true;
+    }
+    return false;
+}
+
+// Every lane of the warp waits for the phase; the result is warp-uniform.
+__device__ __forceinline__ bool warp_wait(std::uint64_t* bar, unsigned parity, volatile int* abort_flag) {
+    const unsigned long long t0 = global_ns();
+    for (unsigned i = 0; i < kMbarMaxPolls; ++i) {
+        const bool done = mbar_try(bar, parity);
+        if (__all_sync(0xffffffffu, done)) return true;
+        if ((i & 63u) == 63u) {
+            int stop = 0;
+            if ((threadIdx.x & 31u) == 0) stop = pipe_stop(abort_flag, t0);
+            if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+        }
+    }
+    if ((threadIdx.x & 31u) == 0) *abort_flag = 1;
+    return false;
+}
+
+__device__ __forceinline__ void warp_arrive(std::uint64_t* bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31u) == 0) mbar_arrive(bar);
+}
+
+// Arrives on the barrier once all of this thread's earlier cp.async copies
+// have landed (the arrival is one of the barrier's expected count).
+__device__ __forceinline__ void cp_async_arrive(std::uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// L2 eviction priorities: the row values a batch re-reads twice (pass B, y)
+// are kept ahead of the data read or written once (the pass-A inputs of the
+// add modes, y), so the re-reads find them in L2 at steady state.
+__device__ __forceinline__ std::uint64_t l2_keep() {
+    std::uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ std::uint64_t l2_stream() {
+    std::uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void cp_async16_l2(void* dst, const void* src, std::uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(smem_addr(dst)), "l"(src),
+                 "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ void st_l2(float4* p, const float4& v, std::uint64_t policy) {
+    asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w), "l"(policy)
+                 : "memory");
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kPipeThreads, 1)
+ln_exact_pipe(LnArgs a) {
     pdl_begin();
-    constexpr int THREADS = kExactThreads, LOADERS = THREADS - 32, U = 8;
-    extern __shared__ __align__(16) float stage_buf[];  // [2][kExactRows][kExactPitch]
-    __shared__ float mean_s[kExactRows], inv_s[kExactRows];
+    constexpr int NIN = pipe_inputs<MODE>();
+    constexpr int S = pipe_stages<MODE>();
+    constexpr int AHEAD = S - 1;  // ticks staged ahead of the one being used
+    constexpr int CW = kPipeComputeWarps;
+    constexpr int Q = kPipeChunk / 4;  // float4 of a row chunk (one per lane)
+    // readers of a stage: the compute warps (y-pass tile, gamma / beta, their
+    // own pass-A copies), chain B (pass-B tile), chain A (plain LN's pass A)
+    constexpr unsigned kStageReaders = CW + (MODE == kLN ? 2u : 1u);
+    extern __shared__ __align__(128) float smem[];
+    __shared__ PipeShared sh;
     const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const std::size_t h = a.h, h4 = h / 4;
-    const int chunks = static_cast<int>((h + kExactChunk - 1) / kExactChunk);
-    const float hf = static_cast<float>(h);
-    const float4* x4 = reinterpret_cast<const float4*>(a.x);
-    for (std::size_t b0 = static_cast<std::size_t>(blockIdx.x) * kExactRows; b0 < a.rows;
-         b0 += static_cast<std::size_t>(gridDim.x) * kExactRows) {
-        const int nr = static_cast<int>(a.rows - b0 < kExactRows ? a.rows - b0 : kExactRows);
-        // copies chunk c of the batch's rows into buffer c & 1; each thread
-        // issues U loads before it stores any, so a chunk costs a few memory
-        // latencies, not one per item
-        auto stage = [&](int c, unsigned first, unsigned stride) {
-            const std::size_t c4 = static_cast<std::size_t>(c) * (kExactChunk / 4);
-            const unsigned len4 = static_cast<unsigned>(min(static_cast<std::size_t>(kExactChunk / 4), h4 - c4));
-            const unsigned total = static_cast<unsigned>(nr) * len4;
-            float4* buf = reinterpret_cast<float4*>(stage_buf + (c & 1) * kExactRows * kExactPitch);
-            for (unsigned it0 = first; it0 < total; it0 += stride * U) {
-                float4 v[U];
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const unsigned it = it0 + u * stride;
-                    if (it < total) v[u] = ld_plain(x4 + (b0 + it / len4) * h4 + c4 + it % len4);
-                }
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const unsigned it = it0 + u * stride;
-                    if (it < total) buf[(it / len4) * (kExactPitch / 4) + it % len4] = v[u];
-                }
-            }
-        };
-        // lane r runs f over row r's elements of chunk c, in ascending order
-        auto chain = [&](int c, auto f) {
-            const std::size_t c4 = static_cast<std::size_t>(c) * (kExactChunk / 4);
-            const unsigned len4 = static_cast<unsigned>(min(static_cast<std::size_t>(kExactChunk / 4), h4 - c4));
-            const float4* row = reinterpret_cast<const float4*>(stage_buf + (c & 1) * kExactRows * kExactPitch +
-                                                                  lane * kExactPitch);
-#pragma unroll 4
-            for (unsigned i = 0; i < len4; ++i) {
-                const float4 v = row[i];
-                f(v.x);
-                f(v.y);
-                f(v.z);
-                f(v.w);
-            }
-        };
-        float acc = 0.0f, mean = 0.0f;
-        for (int pass = 0; pass < 2; ++pass) {
-            stage(0, tid, THREADS);
-            __syncthreads();
-            for (int c = 0; c < chunks; ++c) {
-                if (warp != 0) {
-                    if (c + 1 < chunks) stage(c + 1, tid - 32, LOADERS);
-                } else if (lane < static_cast<unsigned>(nr)) {
-                    if (pass == 0)
-                        chain(c, [&](float x) { acc = __fadd_rn(acc, x); });
-                    else
-                        chain(c, [&](float x) {
-                            const float t = __fsub_rn(x, mean);
-                            acc = __fmaf_rn(t, t, acc);
-                        });
-                }
-                __syncthreads();
-            }
-            if (pass == 0) {
-                mean = __fdiv_rn(acc, hf);
-                acc = 0.0f;
-            }
+    const int NT = static_cast<int>(h / kPipeChunk);
+    const std::size_t total_batches = (a.rows + kPipeRows - 1) / kPipeRows;
+    const int nb = blockIdx.x < total_batches
+                       ? static_cast<int>((total_batches - 1 - blockIdx.x) / gridDim.x + 1)
+                       : 0;
+    const long long G = static_cast<long long>(nb + 2) * NT;  // ticks, two batches of drain
+    volatile int* abort_flag = &sh.abort;
+
+    auto stage_base = [&](int st) { return smem + st * pipe_stage_floats<MODE>(); };
+    auto tile_in = [&](int st, int input) { return stage_base(st) + input * kPipeTile; };
+    auto tile_b = [&](int st) { return stage_base(st) + NIN * kPipeTile; };
+    auto tile_o = [&](int st) { return stage_base(st) + (NIN + 1) * kPipeTile; };
+    auto tile_gb = [&](int st) { return stage_base(st) + (NIN + 2) * kPipeTile; };  // gamma | beta
+    float* svals = smem + S * pipe_stage_floats<MODE>();  // [2] tiles (add modes)
+    auto row0 = [&](int j) {
+        return (static_cast<std::size_t>(blockIdx.x) + static_cast<std::size_t>(j) * gridDim.x) * kPipeRows;
+    };
+    auto nrows = [&](int j) {
+        const std::size_t r = a.rows - row0(j);
+        return static_cast<int>(r < static_cast<std::size_t>(kPipeRows) ? r : kPipeRows);
+    };
+    // the row values passes B and y read: x itself, or the sum written to x_out
+    const float* sval = MODE == kLN ? a.x : a.x_out;
+
+    if (tid == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&sh.full[i], 32 * CW);
+            mbar_init(&sh.empty[i], kStageReaders);
         }
-        if (warp == 0 && lane < static_cast<unsigned>(nr)) {
-            mean_s[lane] = mean;
-            inv_s[lane] = inv_std(acc, hf, a.eps);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sh.sfull[i], CW);
+            mbar_init(&sh.sempty[i], 1);
+            mbar_init(&sh.mfull[i], 1);
+            mbar_init(&sh.mempty[i], 1);
+            mbar_init(&sh.ifull[i], 1);
+            mbar_init(&sh.iempty[i], CW);
         }
-        __syncthreads();
-        // ---- pass C: y for the batch, all threads, coalesced ----
-        const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
-        const float4* be4 = reinterpret_cast<const float4*>(a.beta);
-        const std::size_t total = static_cast<std::size_t>(nr) * h4;
-        for (std::size_t it0 = tid; it0 < total; it0 += THREADS * U) {
-            float4 v[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {  // all loads first
-                const std::size_t it = it0 + static_cast<std::size_t>(u) * THREADS;
-                if (it < total) v[u] = ld_plain(x4 + b0 * h4 + it);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const std::size_t it = it0 + static_cast<std::size_t>(u) * THREADS;
-                if (it >= total) continue;
-                const std::size_t r = it / h4, j = it % h4;
-                st_plain(reinterpret_cast<float4*>(a.y) + b0 * h4 + it,
-                         ln_out4(v[u], mean_s[r], inv_s[r], __ldg(g4 + j), __ldg(be4 + j)));
-            }
-        }
-        __syncthreads();  // mean_s / inv_s and the buffers are reused by the next batch
+        sh.abort = 0;
     }
+    __syncthreads();
+
+    if (warp == 0) {
+        // ---- chain A: ascending sums ----
+        float acc = 0.0f;
+        unsigned q = 0;  // pass-A ticks so far
+        for (long long g = 0; g < G; ++g) {
+            const int st = static_cast<int>(g % S);
+            const unsigned use = static_cast<unsigned>(g / S);
+            const int jb = static_cast<int>(g / NT), c = static_cast<int>(g % NT);
+            if (MODE == kLN && !warp_wait(&sh.full[st], use & 1u, abort_flag)) break;
+            if (jb < nb) {
+                const float* tile;
+                if (MODE == kLN) {
+                    tile = tile_in(st, 0);
+                } else {
+                    if (!warp_wait(&sh.sfull[q & 1u], (q >> 1) & 1u, abort_flag)) break;
+                    tile = svals + (q & 1u) * kPipeTile;
+                }
+                if (static_cast<int>(lane) < nrows(jb)) {
+                    const float4* row = reinterpret_cast<const float4*>(tile + lane * kPipePitch);
+#pragma unroll 8
+                    for (int i = 0; i < Q; ++i) {
+                        const float4 v = row[i];
+                        acc = __fadd_rn(acc, v.x);
+                        acc = __fadd_rn(acc, v.y);
+                        acc = __fadd_rn(acc, v.z);
+                        acc = __fadd_rn(acc, v.w);
+                    }
+                }
+                if (MODE != kLN) warp_arrive(&sh.sempty[q & 1u]);
+                ++q;
+                if (c == NT - 1) {
+                    const float mean = __fdiv_rn(acc, static_cast<float>(h));
+                    acc = 0.0f;
+                    if (!warp_wait(&sh.mempty[jb & 1], ((jb >> 1) & 1) ^ 1, abort_flag)) break;
+                    if (lane < kPipeRows) sh.mean_a[jb & 1][lane] = mean;
+                    warp_arrive(&sh.mfull[jb & 1]);
+                }
+            }
+            if (MODE == kLN) warp_arrive(&sh.empty[st]);
+        }
+    } else if (warp == 1) {
+        // ---- chain B: ascending sums of squared deviations ----
+        float acc = 0.0f, mean = 0.0f;
+        for (long long g = 0; g < G; ++g) {
+            const int st = static_cast<int>(g % S);
+            const unsigned use = static_cast<unsigned>(g / S);
+            const int jb = static_cast<int>(g / NT), c = static_cast<int>(g % NT);
+            const int j = jb - 1;  // batch in pass B
+            if (!warp_wait(&sh.full[st], use & 1u, abort_flag)) break;
+            if (j >= 0 && j < nb) {
+                if (c == 0) {
+                    if (!warp_wait(&sh.mfull[j & 1], (j >> 1) & 1, abort_flag)) break;
+                    mean = lane < kPipeRows ? sh.mean_a[j & 1][lane] : 0.0f;
+                    warp_arrive(&sh.mempty[j & 1]);
+                }
+                if (static_cast<int>(lane) < nrows(j)) {
+                    const float4* row = reinterpret_cast<const float4*>(tile_b(st) + lane * kPipePitch);
+#pragma unroll 8
+                    for (int i = 0; i < Q; ++i) {
+                        const float4 v = row[i];
+                        float t;
+                        t = __fsub_rn(v.x, mean); acc = __fmaf_rn(t, t, acc);
+                        t = __fsub_rn(v.y, mean); acc = __fmaf_rn(t, t, acc);
+                        t = __fsub_rn(v.z, mean); acc = __fmaf_rn(t, t, acc);
+                        t = __fsub_rn(v.w, mean); acc = __fmaf_rn(t, t, acc);
+                    }
+                }
+                if (c == NT - 1) {
+                    const float inv = inv_std(acc, static_cast<float>(h), a.eps);
+                    acc = 0.0f;
+                    if (!warp_wait(&sh.iempty[j & 1], ((j >> 1) & 1) ^ 1, abort_flag)) break;
+                    if (lane < kPipeRows) {
+                        sh.mean_o[j & 1][lane] = mean;
+                        sh.inv_o[j & 1][lane] = inv;
+                    }
+                    warp_arrive(&sh.ifull[j & 1]);
+                }
+            }
+            warp_arrive(&sh.empty[st]);
+        }
+    } else {
+        // ---- compute warps: staging, row values of batch b, y of batch b - 2 ----
+        const int cw = static_cast<int>(warp) - 2;  // rows cw and cw + 8 of each tile, float4 column `lane`
+        const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+        const float4* b4 = reinterpret_cast<const float4*>(a.beta);
+        const float4* sv4 = reinterpret_cast<const float4*>(sval);
+        const float4* x4 = reinterpret_cast<const float4*>(a.x);
+        const float4* r4 = reinterpret_cast<const float4*>(a.res);
+        const float4* e4 = reinterpret_cast<const float4*>(a.expert_out);
+        float4* xo4 = reinterpret_cast<float4*>(a.x_out);
+        float4* y4 = reinterpret_cast<float4*>(a.y);
+        const int o_lane = 4 * static_cast<int>(lane);
+        const std::uint64_t keep = l2_keep(), stream = l2_stream();
+        // expert rows of this thread's two rows (combine mode): of the batch
+        // being staged (is_*), and which of them the batch being formed has (ps_*)
+        std::size_t is_lo[2] = {0, 0}, is_hi[2] = {0, 0};
+        bool is_lok[2] = {false, false}, is_hok[2] = {false, false};
+        bool ps_lok[2] = {false, false}, ps_hok[2] = {false, false};
+        auto expert_rows = [&](int j, int k, std::size_t& lo, std::size_t& hi, bool& lok, bool& hok) {
+            lok = hok = false;
+            if (cw + 8 * k >= nrows(j)) return;
+            const std::size_t t = row0(j) + cw + 8 * k;
+            const std::uint8_t e0 = __ldg(a.routes + 2 * t), e1 = __ldg(a.routes + 2 * t + 1);
+            const std::size_t p0 = __ldg(a.route_positions + 2 * t);
+            const std::size_t p1 = __ldg(a.route_positions + 2 * t + 1);
+            lo = e0 < e1 ? p0 : p1;
+            hi = e0 < e1 ? p1 : p0;
+            lok = lo < a.expert_rows;
+            hok = hi < a.expert_rows;
+        };
+        // stages this thread's part of tick t: the pass-A inputs of batch
+        // t / NT, the pass-B tile of the batch before, the y-pass tile of the
+        // batch before that (and, warps 0 / 1, the gamma / beta chunk)
+        auto stage = [&](long long t) -> bool {
+            if (t >= G) return true;
+            const int st = static_cast<int>(t % S);
+            const unsigned use = static_cast<unsigned>(t / S);
+            const int jb = static_cast<int>(t / NT), c = static_cast<int>(t % NT);
+            if (!warp_wait(&sh.empty[st], (use & 1u) ^ 1u, abort_flag)) return false;
+            const std::size_t c4 = static_cast<std::size_t>(c) * Q + lane;
+            if (jb < nb) {
+                if (MODE == kCombineAddLN && c == 0)
+                    for (int k = 0; k < 2; ++k) {
+                        expert_rows(jb, k, is_lo[k], is_hi[k], is_lok[k], is_hok[k]);
+                        if (lane == 0 && cw + 8 * k < nrows(jb) && (!is_lok[k] || !is_hok[k]))
+                            flag_check(B2_CHECK_COMBINE);
+                    }
+                const int nra = nrows(jb);
+                for (int k = 0; k < 2; ++k) {
+                    const int r = cw + 8 * k;
+                    if (r >= nra) continue;
+                    const std::size_t row = row0(jb) + r;
+                    const int o = r * kPipePitch + o_lane;
+                    if (MODE == kLN) {  // x is the row value: kept for the re-reads
+                        cp_async16_l2(tile_in(st, 0) + o, x4 + row * h4 + c4, keep);
+                    } else if (MODE == kAddLN) {
+                        cp_async16_l2(tile_in(st, 0) + o, x4 + row * h4 + c4, stream);
+                        cp_async16_l2(tile_in(st, 1) + o, r4 + row * h4 + c4, stream);
+                    } else {
+                        cp_async16_l2(tile_in(st, 0) + o, r4 + row * h4 + c4, stream);
+                        if (is_lok[k]) cp_async16_l2(tile_in(st, 1) + o, e4 + is_lo[k] * h4 + c4, stream);
+                        if (is_hok[k]) cp_async16_l2(tile_in(st, 2) + o, e4 + is_hi[k] * h4 + c4, stream);
+                    }
+                }
+            }
+            if (jb >= 1 && jb - 1 < nb) {
+                const int nrb = nrows(jb - 1);
+                for (int k = 0; k < 2; ++k) {
+                    const int r = cw + 8 * k;
+                    if (r < nrb)
+                        cp_async16_l2(tile_b(st) + r * kPipePitch + o_lane, sv4 + (row0(jb - 1) + r) * h4 + c4,
+                                      keep);
+                }
+            }
+            if (jb >= 2 && jb - 2 < nb) {
+                const int nro = nrows(jb - 2);
+                for (int k = 0; k < 2; ++k) {
+                    const int r = cw + 8 * k;
+                    if (r < nro)  // the last read of these row values
+                        cp_async16_l2(tile_o(st) + r * kPipePitch + o_lane, sv4 + (row0(jb - 2) + r) * h4 + c4,
+                                      stream);
+                }
+                if (cw < 2) cp_async16(tile_gb(st) + cw * kPipeChunk + o_lane, (cw == 0 ? g4 : b4) + c4);
+            }
+            cp_async_arrive(&sh.full[st]);
+            return true;
+        };
+        float m_o[2] = {0.f, 0.f}, i_o[2] = {0.f, 0.f};
+        bool ok = true;
+        for (int d = 0; d < AHEAD && ok; ++d) ok = stage(d);
+        unsigned q = 0;
+        for (long long g = 0; g < G && ok; ++g) {
+            if (!stage(g + AHEAD)) break;
+            const int st = static_cast<int>(g % S);
+            const unsigned use = static_cast<unsigned>(g / S);
+            const int jb = static_cast<int>(g / NT), c = static_cast<int>(g % NT);
+            const int jo = jb - 2;  // batch whose y this tick writes
+            if (!warp_wait(&sh.full[st], use & 1u, abort_flag)) break;
+            if (MODE != kLN && jb < nb) {
+                if (MODE == kCombineAddLN && c == 0) {
+                    std::size_t lo, hi;
+                    for (int k = 0; k < 2; ++k) expert_rows(jb, k, lo, hi, ps_lok[k], ps_hok[k]);
+                }
+                if (!warp_wait(&sh.sempty[q & 1u], ((q >> 1) & 1u) ^ 1u, abort_flag)) break;
+                const int nra = nrows(jb);
+                float* tile = svals + (q & 1u) * kPipeTile;
+                const std::size_t c4 = static_cast<std::size_t>(c) * Q + lane;
+                for (int k = 0; k < 2; ++k) {
+                    const int r = cw + 8 * k;
+                    if (r >= nra) continue;
+                    const int o = r * kPipePitch + o_lane;
+                    const float4 v0 = *reinterpret_cast<const float4*>(tile_in(st, 0) + o);
+                    float4 v;
+                    if (MODE == kAddLN) {
+                        v = add4(v0, *reinterpret_cast<const float4*>(tile_in(st, 1) + o));
+                    } else {
+                        const float4 lo4 = ps_lok[k] ? *reinterpret_cast<const float4*>(tile_in(st, 1) + o) : zero4();
+                        const float4 hi4 = ps_hok[k] ? *reinterpret_cast<const float4*>(tile_in(st, 2) + o) : zero4();
+                        v = add4(combine4(lo4, hi4), v0);
+                    }
+                    st_l2(xo4 + (row0(jb) + r) * h4 + c4, v, keep);
+                    *reinterpret_cast<float4*>(tile + o) = v;
+                }
+                warp_arrive(&sh.sfull[q & 1u]);
+                ++q;
+            }
+            if (jo >= 0 && jo < nb) {
+                if (c == 0) {
+                    if (!warp_wait(&sh.ifull[jo & 1], (jo >> 1) & 1, abort_flag)) break;
+                    for (int k = 0; k < 2; ++k) {
+                        m_o[k] = sh.mean_o[jo & 1][cw + 8 * k];
+                        i_o[k] = sh.inv_o[jo & 1][cw + 8 * k];
+                    }
+                    warp_arrive(&sh.iempty[jo & 1]);
+                }
+                const float4 gw = *reinterpret_cast<const float4*>(tile_gb(st) + o_lane);
+                const float4 bw = *reinterpret_cast<const float4*>(tile_gb(st) + kPipeChunk + o_lane);
+                const std::size_t c4 = static_cast<std::size_t>(c) * Q + lane;
+                const int nro = nrows(jo);
+                for (int k = 0; k < 2; ++k) {
+                    const int r = cw + 8 * k;
+                    if (r < nro) {
+                        const float4 v = *reinterpret_cast<const float4*>(tile_o(st) + r * kPipePitch + o_lane);
+                        st_l2(y4 + (row0(jo) + r) * h4 + c4, ln_out4(v, m_o[k], i_o[k], gw, bw), stream);
+                    }
+                }
+            }
+            warp_arrive(&sh.empty[st]);
+        }
+        cp_async_wait_all();  // no copy may land after the CTA has gone
+    }
+    __syncthreads();
 }
 
 constexpr std::size_t kMaxSmemRow = 220 * 1024;  // + static reduction slots <= 227 KB
@@ -478,13 +799,15 @@ int launch_reg(const LnArgs& a, cudaStream_t s) {
     return B2_OK;
 }
 
-int launch_exact_batch(const LnArgs& a, cudaStream_t s) {
-    const std::size_t smem = 2 * kExactRows * kExactPitch * sizeof(float);
-    if (allow_dynamic_smem(reinterpret_cast<const void*>(ln_exact_batch), smem) != cudaSuccess)
+template <int MODE>
+int launch_exact_pipe(const LnArgs& a, cudaStream_t s) {
+    constexpr std::size_t smem = pipe_smem<MODE>();
+    auto kernel = ln_exact_pipe<MODE>;
+    if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
         return launch_result("layer norm: shared memory attribute");
-    const std::size_t batches = (a.rows + kExactRows - 1) / kExactRows;
-    const unsigned grid = static_cast<unsigned>(batches < static_cast<std::size_t>(sm_count()) ? batches : sm_count());
-    launch_pdl(ln_exact_batch, grid, kExactThreads, smem, s, a);
+    const std::size_t batches = (a.rows + kPipeRows - 1) / kPipeRows;
+    const std::size_t sms = static_cast<std::size_t>(sm_count());
+    launch_pdl(kernel, static_cast<unsigned>(batches < sms ? batches : sms), kPipeThreads, smem, s, a);
     return B2_OK;
 }
 
@@ -511,18 +834,23 @@ int launch_smem(const LnArgs& a, cudaStream_t s) {
     return B2_OK;
 }
 
-// Picks, for plain LayerNorm in reference order over at least 32 rows per
-// SM, the 32-row batched kernel; otherwise the register-resident variant
-// whose THREADS * V covers h / 4, else bulk-copy staging (aligned rows,
+// Picks, in reference order over enough rows (h a multiple of 128, aligned),
+// the chain pipeline; otherwise the register-resident variant whose
+// THREADS * V covers h / 4, else bulk-copy staging (aligned rows,
 // h % 4 == 0), else the scalar shared-memory one.
+constexpr int kPipeMinBatchesPerSm = 4;
 template <int MODE>
 int dispatch(const LnArgs& a, bool exact, bool vec_ok, cudaStream_t s, const char* what) {
     if (a.h * sizeof(float) > kMaxSmemRow && exact)
         return set_error(B2_ERR_UNSUPPORTED, std::string(what) + ": h too large");
     int rc = B2_OK;
     const std::size_t h4 = a.h / 4;
-    if (MODE == kLN && vec_ok && exact && a.rows >= static_cast<std::size_t>(kExactRows) * sm_count()) {
-        rc = launch_exact_batch(a, s);  // enough rows for a 32-row batch on every SM
+    // (h >= pipe_stages chunks in the add modes: a thread's copies of the
+    // x_out chunks it wrote are then staged after it wrote them)
+    if (vec_ok && exact && a.h % kPipeChunk == 0 &&
+        a.h >= static_cast<std::size_t>(MODE == kLN ? 1 : pipe_stages<MODE>()) * kPipeChunk &&
+        a.rows >= static_cast<std::size_t>(kPipeMinBatchesPerSm) * kPipeRows * sm_count()) {
+        rc = launch_exact_pipe<MODE>(a, s);  // enough 16-row batches for the pipeline to fill
     } else if (vec_ok && !exact && h4 <= 256 * 8) {
         if (h4 <= 256) rc = launch_reg<MODE, 256, 1, false>(a, s);
         else if (h4 <= 512) rc = launch_reg<MODE, 256, 2, false>(a, s);

@@ -37,9 +37,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "non-GEMM prefill tokens/s (64x2048 prompts, 32 layers; layer-op HBM GB/s in roofline)"
 # DRAM bytes (read + write) per node row of a kernel launch, from one ncu
-# capture of that kernel on a smaller case of the same workload (8192 rows),
+# capture of that kernel on a smaller case of the same workload (32,768 rows),
 # scaled to a launch by rows.
-TRAFFIC_BYTES_PER_ROW = {"fused": (402.782208e6 + 212.583936e6) / 8192}
+TRAFFIC_BYTES_PER_ROW = {"fused": (1611.028480e6 + 1017.303808e6) / 32768}
 
 
 def parse():

@@ -70,10 +70,14 @@ def test_gather_rows_empty_and_bad_index(ops, cuda, h):
 
 # register rows (h <= 8192 tree order, <= 4096 exact order), bulk-copy staged
 # rows (aligned, h % 4 == 0, longer), scalar staged rows (h % 4 != 0); in
-# exact order, plain LayerNorm over >= 32 rows per SM takes the 32-row batched
-# kernel (partial last batch, partial last chunk at h = 4100)
+# exact order, >= 4 16-row batches per SM (9,472 rows on 148 SMs) with h a
+# multiple of 128 (and, with a residual, at least as many chunks as ring
+# stages) take the chain pipeline: a 1-row last batch (9473), h at the add
+# modes' minimum (640), an odd chunk count (1152), and many batches per CTA
+# (20000)
+PIPE_SHAPES = [(9473, 4096), (9500, 640), (9488, 1152), (20000, 1024)]
 LN_SHAPES = [(512, 4096), (7, 4096), (3, 100), (5, 4100), (2, 12288), (1, 8192), (4, 2048), (3, 16384),
-             (2, 37), (4800, 4096), (5003, 4100)]
+             (2, 37), (4800, 4096), (5003, 4100)] + PIPE_SHAPES
 
 
 @pytest.mark.parametrize("rows,h", LN_SHAPES)
@@ -329,7 +333,7 @@ def test_moe_combine_bitexact(ops, cuda, T, h):
     oracle.assert_bitexact(to_host(out), oracle.moe_combine(eo, r["routes"], r["route_positions"], T), "combine")
 
 
-@pytest.mark.parametrize("T,h", [(4096, 4096), (5, 100), (3, 12288), (6, 8192), (4801, 4096)])
+@pytest.mark.parametrize("T,h", [(4096, 4096), (5, 100), (3, 12288), (6, 8192), (4801, 4096)] + PIPE_SHAPES)
 @pytest.mark.parametrize("exact", [False, True])
 def test_moe_combine_add_layer_norm(ops, cuda, T, h, exact):
     import torch

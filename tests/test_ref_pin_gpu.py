@@ -60,7 +60,8 @@ def test_ref_gather(ops, cuda):
     oracle.assert_bitexact(to_host(out), to_host(ref_out), "b2 vs ref gather")
 
 
-@pytest.mark.parametrize("rows,h", [(512, 4096), (9, 100), (3, 4100)])
+# 9473 x 4096: the exact-order chain pipeline (>= 9,472 rows), 1-row last batch
+@pytest.mark.parametrize("rows,h", [(512, 4096), (9, 100), (3, 4100), (9473, 4096)])
 def test_ref_layer_norm(ops, cuda, rows, h):
     import torch
 
@@ -82,7 +83,7 @@ def test_ref_layer_norm(ops, cuda, rows, h):
             oracle.assert_close(to_host(y), ry, what="b2 vs ref LN")
 
 
-@pytest.mark.parametrize("rows,h", [(512, 4096), (5, 36)])
+@pytest.mark.parametrize("rows,h", [(512, 4096), (5, 36), (9473, 4096)])
 def test_ref_add_layer_norm(ops, cuda, rows, h):
     import torch
 
