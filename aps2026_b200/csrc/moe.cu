@@ -23,7 +23,6 @@
 //      all CTAs together write the two work queues.
 // Token order within an expert is ascending, exactly what
 // k_moe_fill_stable produces; all integer outputs are bit-identical.
-#include <mutex>
 #include <string>
 
 #include "fastexp.cuh"
@@ -598,28 +597,17 @@ namespace {
 constexpr std::size_t kNoAllocScratchWords = 32768;
 static __device__ __align__(256) std::uint32_t g_route_scratch[kNoAllocScratchWords];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-std::uint32_t* g_scratch_addr[kMaxDevices] = {};
-
-// Device address of g_route_scratch on the current device, looked up once
-// per device (in host code the array's name is not a device address).
+// Device address of g_route_scratch in the current device's context (in
+// host code the array's name is not a device address). Looked up on every
+// call rather than cached: a context torn down and created again
+// (cudaDeviceReset) may hold the array at another address.
 int route_scratch_address(std::uint32_t** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_route_scratch);
     if (e != cudaSuccess)
-        return set_error(B2_ERR_CUDA, std::string("b2_moe_route_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
-    if (dev < 0 || dev >= kMaxDevices) return set_error(B2_ERR_UNSUPPORTED, "b2_moe_route_noalloc: device index");
-    std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_addr[dev]) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_route_scratch);
-        if (e != cudaSuccess)
-            return set_error(B2_ERR_CUDA,
-                             std::string("b2_moe_route_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-        g_scratch_addr[dev] = static_cast<std::uint32_t*>(p);
-    }
-    *out = g_scratch_addr[dev];
+        return set_error(B2_ERR_CUDA,
+                         std::string("b2_moe_route_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    *out = static_cast<std::uint32_t*>(p);
     return B2_OK;
 }
 

@@ -270,8 +270,10 @@ int b2_moe_route(const float* logits, size_t T, size_t E, float quantum,
  * 128 KB array compiled into the library (held by every GPU that loads it
  * until the process exits), which limits ceil(T/256) * E' to 32768 words
  * with E' = E rounded up to a power of two >= 4 (524,288 tokens at E = 16);
- * larger requests return B2_ERR_UNSUPPORTED. The first call on a device looks
- * up the array's device address (cudaGetSymbolAddress); make that first call
+ * larger requests return B2_ERR_UNSUPPORTED. Each call looks up the array's
+ * device address on the current device (cudaGetSymbolAddress, a host-side
+ * lookup), so a context reset between calls is safe; the first call on a
+ * device also loads the library's device code there, so make that first call
  * before any stream capture. All calls on a device share the array: calls
  * that overlap on the GPU (other streams, other host threads) race on it.
  * Every word a call reads it has written first, so nothing needs clearing.

@@ -5,9 +5,12 @@ array inside the library, so it takes no workspace argument.
 
 Called through the C ABI and checked against b2_moe_route (caller
 workspace) on the same logits: the outputs are integer indices, so they must
-agree bit for bit -- on two calls in a row, the second smaller than the
-first, so stale scratch contents from the first call are exercised. This
-file is collected last on purpose."""
+agree bit for bit -- on calls in a row, each smaller than the one before, so
+stale scratch contents from the earlier calls are exercised. The cases reach
+every padded expert width of the histogram reduction (E' = 4, 16, 32) and
+the largest size the fixed scratch accepts (524,288 tokens at E = 16); one
+case is also checked against the CPU oracle. This file is collected last on
+purpose."""
 import ctypes as C
 
 import numpy as np
@@ -41,11 +44,15 @@ def _route(lib, fn_name, logits, ws=None):
 def test_noalloc_route_matches_workspace_route_twice(cuda):
     import torch
 
+    import oracle
     from aps2026_b200 import _lib, ops
 
     lib = _lib.lib()
     g = np.random.default_rng(77)
-    for T, E in ((100_003, 16), (3_000, 13)):
+    # largest first: 524,288 tokens at E = 16 fill the fixed scratch exactly
+    # (2048 tiles x 16 words); E = 32 and E = 3 take the E' = 32 and E' = 4
+    # histogram paths
+    for T, E in ((524_288, 16), (100_003, 16), (70_001, 32), (5_000, 3), (3_000, 13)):
         logits = torch.from_numpy(g.standard_normal((T, E)).astype(np.float32)).to(cuda)
         rc_a, a = _route(lib, "b2_moe_route_noalloc", logits)
         assert rc_a == 0, _lib.last_error()
@@ -54,6 +61,10 @@ def test_noalloc_route_matches_workspace_route_twice(cuda):
         for name in ("routes", "counts", "offsets", "assignment_rows", "route_positions", "work_expert64",
                      "work_start64", "work_expert128", "work_start128"):
             assert torch.equal(getattr(a, name), getattr(b, name)), f"T={T} E={E}: {name} differs"
+        if (T, E) == (5_000, 3):
+            want = oracle.moe_route(logits.cpu().numpy())
+            for name in ("assignment_rows", "route_positions"):
+                assert np.array_equal(getattr(a, name).cpu().numpy().view(np.uint32), want[name]), name
 
 
 def test_noalloc_route_rejects_sizes_beyond_its_scratch(cuda):
