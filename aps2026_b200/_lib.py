@@ -39,6 +39,7 @@ SIGNATURES: dict[str, tuple] = {
     "b2_prefix_trie_device": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "b2_layer_norm": (C.c_int, [_vp, _vp, _vp, _vp, _sz, _sz, _f32, _u32, _vp]),
     "b2_add_layer_norm": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _sz, _sz, _f32, _u32, _vp]),
+    "b2_layer_norm_stats": (C.c_int, [_vp, _sz, _sz, _f32, _u32, _vp, _vp, _vp]),
     "b2_moe_combine_add_layer_norm": (
         C.c_int, [_vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _f32, _u32, _vp]),
     "b2_rope_table": (C.c_int, [_sz, _sz, _f32, _vp, _vp]),

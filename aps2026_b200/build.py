@@ -37,7 +37,7 @@ def _sources() -> list[Path]:
 
 
 def _headers() -> list[Path]:
-    return sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+    return sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h")) + sorted(INCLUDE.glob("*.cuh"))
 
 
 def _compile(src: Path, verbose: bool) -> Path:

@@ -10,6 +10,7 @@
 #include <string>
 
 #include "../../include/aps2026_b200.h"
+#include "../../include/aps2026_b200_fusion.cuh"
 
 namespace b2 {
 

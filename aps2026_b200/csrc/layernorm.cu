@@ -57,8 +57,10 @@ __device__ __forceinline__ float sqdev4(const float4& v, float m) {
     return __fadd_rn(__fmaf_rn(a, a, __fmul_rn(b, b)), __fmaf_rn(c, c, __fmul_rn(d, d)));
 }
 
+// the public prologue hook of aps2026_b200_fusion.cuh: a GEMM that forms
+// its operand with it matches this kernel's output bit for bit
 __device__ __forceinline__ float ln_out(float s, float mean, float inv, float w, float b) {
-    return __fmaf_rn(__fmul_rn(__fsub_rn(s, mean), inv), w, b);
+    return b2_fusion::layer_norm_value(s, mean, inv, w, b);
 }
 
 __device__ __forceinline__ float4 ln_out4(const float4& s, float mean, float inv,
@@ -786,6 +788,48 @@ ln_exact_pipe(LnArgs a) {
     __syncthreads();
 }
 
+// Per-row statistics only (b2_layer_norm_stats): the mean and 1/std every
+// LayerNorm kernel here forms, for a GEMM that applies the normalisation in
+// its prologue. CTA per row (grid-stride), the row staged in shared memory;
+// reference order: thread 0's serial ascending sums (serial_moments, as the
+// exact kernels), otherwise a block tree reduction.
+template <bool EXACT>
+__global__ void __launch_bounds__(128)
+ln_row_stats(const float* x, std::size_t rows, std::size_t h, float eps, float* mean_out, float* inv_out) {
+    pdl_begin();
+    constexpr int THREADS = 128, WARPS = 4;
+    __shared__ float red[2][WARPS];
+    __shared__ float stats[2];
+    extern __shared__ __align__(16) float staged[];
+    const float hf = static_cast<float>(h);
+    for (std::size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        for (std::size_t j = threadIdx.x; j < h; j += THREADS) staged[j] = x[r * h + j];
+        __syncthreads();
+        float mean, inv;
+        if (EXACT) {
+            if (threadIdx.x == 0) serial_moments(staged, h, eps, &stats[0], &stats[1]);
+            __syncthreads();
+            mean = stats[0];
+            inv = stats[1];
+        } else {
+            float part = 0.0f;
+            for (std::size_t j = threadIdx.x; j < h; j += THREADS) part = __fadd_rn(part, staged[j]);
+            mean = __fdiv_rn(block_sum<WARPS>(part, red[0]), hf);
+            float part2 = 0.0f;
+            for (std::size_t j = threadIdx.x; j < h; j += THREADS) {
+                const float t = __fsub_rn(staged[j], mean);
+                part2 = __fmaf_rn(t, t, part2);
+            }
+            inv = inv_std(block_sum<WARPS>(part2, red[1]), hf, eps);
+        }
+        if (threadIdx.x == 0) {
+            mean_out[r] = mean;
+            inv_out[r] = inv;
+        }
+        __syncthreads();  // staged[] and stats are reused by the next row
+    }
+}
+
 constexpr std::size_t kMaxSmemRow = 220 * 1024;  // + static reduction slots <= 227 KB
 
 template <int MODE, int THREADS, int V, bool EXACT>
@@ -901,6 +945,23 @@ int b2_layer_norm(const float* x, const float* gamma, const float* beta, float* 
     const bool vec = (h & 3u) == 0 && all_aligned({x, gamma, beta, y});
     return dispatch<kLN>(a, (flags & B2_FLAG_EXACT_ORDER) != 0, vec, as_stream(stream),
                          "b2_layer_norm");
+}
+
+int b2_layer_norm_stats(const float* x, size_t rows, size_t h, float eps, uint32_t flags, float* mean,
+                        float* inv, b2_stream_t stream) {
+    using namespace b2;
+    if (rows == 0) return B2_OK;
+    if (!x || !mean || !inv) return invalid("layer norm stats: null pointer");
+    if (h == 0) return invalid("layer norm stats shape");
+    const std::size_t smem = h * sizeof(float);
+    if (smem > kMaxSmemRow) return set_error(B2_ERR_UNSUPPORTED, "b2_layer_norm_stats: h too large");
+    const bool exact = (flags & B2_FLAG_EXACT_ORDER) != 0;
+    auto kernel = exact ? ln_row_stats<true> : ln_row_stats<false>;
+    if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
+        return launch_result("b2_layer_norm_stats: shared memory attribute");
+    const unsigned grid = wave_grid(reinterpret_cast<const void*>(kernel), 128, smem, rows);
+    launch_pdl(kernel, grid, 128, smem, as_stream(stream), x, rows, h, eps, mean, inv);
+    return launch_result("b2_layer_norm_stats");
 }
 
 int b2_add_layer_norm(float* x, const float* residual, const float* gamma, const float* beta,

@@ -24,14 +24,12 @@ namespace {
 // one row per step, consecutive CTAs stream consecutive rows.
 constexpr int kRopeRowsPerStep = 1;
 
-// out0 = x0 * c - x1 * s, out1 = x1 * c + x0 * s, with the multiply-adds
-// fused the way nvcc fuses the reference's expressions in k_rope:
-// fma(x0, c, -(x1 * s)) and fma(x0, s, x1 * c).
+// out0 = x0 * c - x1 * s, out1 = x1 * c + x0 * s, fused the way nvcc fuses
+// the reference's expressions in k_rope -- the public epilogue hook of
+// aps2026_b200_fusion.cuh, so a GEMM epilogue built on it rotates exactly
+// as this kernel does.
 __device__ __forceinline__ void rotate(float& x0, float& x1, float c, float s) {
-    const float a = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
-    const float b = __fmaf_rn(x0, s, __fmul_rn(x1, c));
-    x0 = a;
-    x1 = b;
+    b2_fusion::rope_rotate(x0, x1, c, s);
 }
 
 struct RopeArgs {

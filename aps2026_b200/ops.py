@@ -123,6 +123,18 @@ def layer_norm_gpu(x, weight, bias, eps: float, y, exact: bool = False) -> None:
                                     _flags(exact), _stream()), "layer_norm_gpu")
 
 
+def layer_norm_stats_gpu(x, eps: float, exact: bool = False):
+    """Per-row mean and 1/std of x [rows, h] as b2_layer_norm forms them
+    (b2_layer_norm_stats; the operand statistics of a GEMM prologue that
+    applies b2_fusion::layer_norm_value). Returns (mean, inv), fp32 [rows]."""
+    rows, h = _rows_h(x)
+    mean = torch.empty(rows, dtype=torch.float32, device=x.device)
+    inv = torch.empty(rows, dtype=torch.float32, device=x.device)
+    _check(_lib.lib().b2_layer_norm_stats(_f32(x), rows, h, eps, _flags(exact), _ptr(mean), _ptr(inv), _stream()),
+           "layer_norm_stats_gpu")
+    return mean, inv
+
+
 def add_layer_norm_gpu(x, residual, weight, bias, eps: float, y, exact: bool = False) -> None:
     """x += residual; y = LayerNorm(x) (tensor_ops::add_layer_norm_gpu,
     include/tensor.h:88-90)."""

@@ -63,6 +63,7 @@ def parse():
                    help="comma-separated shares of a rank's tokens per sub-batch, in order (default with the "
                         "default 3 chunks at N > 1: 0.5,0.375,0.125; otherwise balanced)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-attention", action="store_true", help="skip the attention-core line")
     p.add_argument("--no-kernel-timing", action="store_true",
                    help="no per-launch events in the timed region (diagnostic; the line then lacks kernels/roofline)")
     p.add_argument("--config", type=int, default=5, choices=[1, 2, 3, 4, 5],
@@ -335,6 +336,49 @@ def run_ours(args):
                       "what": "the same step in B2_FLAG_EXACT_ORDER (the reference's serial LayerNorm sums and "
                               "exponential; bit-identical to the reference kernels), device-resident inputs"}
 
+    # the attention core (softmax included) over this rank's trie rows, one
+    # layer's worth: the one contraction between the non-GEMM ops, reported
+    # beside the step (GEMM outputs are stand-ins, so it is not in the step)
+    att_line = None
+    if not args.no_attention:
+        from aps2026_b200 import ops as _ops
+
+        att_ms, att_keys = 0.0, 0
+        for c, pipe in enumerate(runner.pipes):
+            ps = runner.prompts[c]
+            offs = np.zeros(len(ps) + 1, np.int32)
+            offs[1:] = np.cumsum([len(p) for p in ps])
+            offs_d = torch.from_numpy(offs).to(dev)
+            dt = _ops.prefix_trie_device(torch.from_numpy(np.concatenate(ps).astype(np.int32)).to(dev), offs_d)
+            s0 = pipe._standins[0]
+            q, kv = s0.q, s0.k  # stand-ins of the chunk's q and k; k doubles as v
+            out = torch.empty_like(q)
+            att_keys += int(torch.clamp(dt.node_depth.long() + 1, max=_ops.SLIDING_WINDOW).sum().item())
+
+            def launch():
+                _ops.attention_tree_compact_gpu(q, kv, kv, out, dt.node_depth, dt.node_prompt, offs_d,
+                                                dt.token_node, int(max(len(p) for p in ps)), dt.nodes,
+                                                prefill.Q_HEADS, prefill.KV_HEADS, prefill.HEAD_DIM)
+            launch()
+            aev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            aev[0].record(stream)
+            launch()
+            aev[1].record(stream)
+            launch()
+            aev[2].record(stream)
+            torch.cuda.synchronize()
+            att_ms += min(aev[0].elapsed_time(aev[1]), aev[1].elapsed_time(aev[2]))
+            del out, dt
+        flops = 2 * 2 * prefill.Q_HEADS * prefill.HEAD_DIM * att_keys  # QK and PV multiply-adds per (row, key)
+        fp32_peak = 148 * 128 * 2 * 1965e6 / 1e12
+        att_line = {"kernel": "attention_tree_block (compact chains, tree order)", "ms_per_layer": round(att_ms, 3),
+                    "flops_per_layer": flops, "achieved": round(flops / (att_ms * 1e-3) / 1e12, 2),
+                    "unit": "TFLOP/s", "bound": "fp32", "peak": round(fp32_peak, 1),
+                    "frac": round(flops / (att_ms * 1e-3) / 1e12 / fp32_peak, 3),
+                    "peak_kind": "nominal FP32 CUDA-core rate (148 SMs x 128 lanes x 2 flops x 1965 MHz)",
+                    "per_step_ms_32_layers": round(32 * att_ms, 1),
+                    "what": "this rank's rows, one layer, timed after the timed region; not part of `value`"}
+
     clk = clocks.summary()
     allclk = [clk]
     if dist:
@@ -389,6 +433,7 @@ def run_ours(args):
             "e2e": {"value": round(tokens_total / (e2e_ms / 1e3), 1), "unit": "tokens/s",
                     "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h},
             "exact_order": exact_line,
+            "attention_core": att_line,
             "gpu_launches": runner.launches_per_step() * args.steps * world,
             "standin_gen_s": round(t_gen, 2),
         }

@@ -122,6 +122,21 @@ int b2_layer_norm(const float* x, const float* gamma, const float* beta,
                   b2_stream_t stream);
 
 /*
+ * The per-row statistics of b2_layer_norm without its output: mean[r] and
+ * inv[r] = 1 / sqrtf(var / h + eps) of x[r, :] (x: [rows, h]; mean, inv:
+ * [rows] floats). No reference counterpart as an entry point: they are the
+ * moments k_layer_norm forms internally (ln_moments, src/tensor.cu:2063-2128),
+ * exposed so that a GEMM can normalise its operand in its prologue
+ * (b2_fusion::layer_norm_value, include/aps2026_b200_fusion.cuh) instead of
+ * reading b2_layer_norm's output. With B2_FLAG_EXACT_ORDER they are the
+ * reference's serial sums, bit-identical to what b2_layer_norm uses;
+ * otherwise a tree reduction, within tolerance.
+ */
+int b2_layer_norm_stats(const float* x, size_t rows, size_t h, float eps,
+                        uint32_t flags, float* mean, float* inv,
+                        b2_stream_t stream);
+
+/*
  * x[r, :] += residual[r, :] (written back), then y = LayerNorm(x).
  * Replaces tensor_ops::add_layer_norm_gpu (include/tensor.h:88-90;
  * src/tensor.cu:3282-3295; kernel k_add_layer_norm :2144-2178).
