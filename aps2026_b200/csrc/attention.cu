@@ -29,6 +29,8 @@
 // equivalent): 2 * 4 * window * head_dim multiply-adds per CTA.
 #include "common.cuh"
 #include "fastexp.cuh"
+#include "rowload.cuh"
+#include "tcgen05.cuh"
 
 namespace b2 {
 namespace {
@@ -51,6 +53,7 @@ struct AttnArgs {
     const std::uint32_t* prompt_off;   // [prompts + 1]
     const std::uint32_t* token_node;   // [total]
     std::size_t prompts, total;
+    int tc_paths;                      // attention_tree_tc ran: path blocks of 32 rows are done
 };
 
 // First key of the ancestor chain of row n at position pos (its keys are
@@ -243,6 +246,412 @@ attention_tree_kernel(AttnArgs a) {
     for (int d = tid; d < HD; d += kAttnThreads)
 #pragma unroll
         for (int g = 0; g < kGroup; ++g) out_row[g * HD + d] = value[g];
+}
+
+// ---- tensor-core attention core (tree-order mode, head_dim 128) -------------
+//
+// The default (tree-order) mode only has to land within 1e-5 relative OR
+// 1e-6 absolute of the reference, so its contractions run on the tcgen05
+// tensor cores with FP32-level products: every operand x is split into
+// hi = x rounded to TF32 and lo = (x - hi) rounded to TF32, and each product
+// is lo.hi + hi.lo + hi.hi -- three kind::tf32 MMAs into one FP32
+// accumulator in tensor memory (relative error ~2^-22 per product).
+//
+// One CTA per (block of 32 consecutive trie rows that form a path, KV head):
+// M = 32 rows x 4 query heads = 128 rows of the MMA, and the keys of every
+// row are a prefix of the deepest row's chain, so each 32-key tile of that
+// chain is staged once for all 128 rows.
+//   tensor memory  Q hi / lo [128 x 128] (the A operand of S = Q K^T), S
+//                  [128 x 32] twice, P hi / lo [128 x 32] (the A operand of
+//                  P V), the tile's P V [128 x 128];
+//   shared memory  a ring of 3 key tiles hi / lo [32 keys x 128 dims] and a
+//                  ring of 2 value tiles transposed, hi / lo [128 dims x 32
+//                  keys], K-major in the 128-byte swizzle layout; O [128
+//                  dims][128 MMA rows].
+// Warp roles: 4-5 stage key tiles, 6-7 value tiles (global loads, the
+// split, swizzled stores); 8 issues the MMAs -- S(t + 2) as soon as S(t) has
+// been read, P V(t) once P(t) is written; 0-3 own one MMA row each (thread
+// m: row m / 4 of the block, query head m % 4 of the group, tensor-memory
+// lane m) and run the softmax online: per tile, the row's running maximum m
+// and sum l are updated (l = l * exp(m_old - m) + sum p, p = expf(s * scale
+// - m), 0 outside the row's window), and the previous tile's P V is folded
+// into O as O = O * exp(m_old - m) + PV in FP32 round-to-nearest (the
+// tensor core's accumulator truncates; chaining every tile there biased long
+// windows by ~1e-6). The epilogue writes O * (1 / l): the softmax of the
+// tree-order SIMT kernel, formed in another order. Blocks that are not a
+// path (prompt boundaries, shared-prefix branch points) are left to
+// attention_tree_block, which skips the path blocks by the same test.
+constexpr int kTcRows = 32;  // trie rows per CTA (x 4 heads = M 128)
+constexpr int kTcKeys = 32;  // chain keys per tile
+constexpr int kTcSoftmaxThreads = 128;                      // warps 0-3
+constexpr int kTcStageThreads = 64;                         // warps 4-5 (keys), 6-7 (values)
+constexpr int kTcThreads = kTcSoftmaxThreads + 2 * kTcStageThreads + 32;  // + warp 8 (MMA)
+constexpr int kTcKStages = 3, kTcVStages = 2;
+constexpr std::uint32_t kColQh = 0, kColQl = 128, kColO = 256, kColS = 384, kColPh = 448, kColPl = 480;
+constexpr std::uint32_t kTcCols = 512;
+constexpr int kTcTileBytes = 16 * 1024;  // one operand tile: 32 x 128 or 128 x 32 fp32
+constexpr int kTcStageBytes = 2 * kTcTileBytes;  // hi, lo
+// rings + O + 1024-byte alignment (225 KB: one CTA per SM, each allocating
+// all 512 tensor-memory columns)
+constexpr std::size_t kTcSmem = (kTcKStages + kTcVStages) * kTcStageBytes + 128 * 128 * 4 + 1024;
+
+// Whether rows n0 .. n0 + nr - 1 form a path whose chains are prefixes of the
+// last row's chain: consecutive positions, each row found in the last row's
+// chain at its own position. Evaluated by one full warp; on success *chain
+// and *pos0 describe the block.
+__device__ __forceinline__ bool tc_block_is_path(const AttnArgs& a, std::size_t n0, int nr,
+                                                 const std::uint32_t** chain, std::size_t* pos0) {
+    const unsigned lane = threadIdx.x & 31u;
+    const std::size_t n1 = n0 + nr - 1;
+    const std::size_t p1 = a.row_pos[n1];
+    const std::uint32_t* c = chain_of(a, n1, p1);
+    const std::size_t p0 = a.row_pos[n0];
+    bool ok = c != nullptr && p1 == p0 + static_cast<std::size_t>(nr - 1);
+    if (ok && static_cast<int>(lane) < nr) {
+        const std::size_t pi = a.row_pos[n0 + lane];
+        ok = pi == p0 + lane && c[pi] == n0 + lane;
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    *chain = c;
+    *pos0 = p0;
+    return ok;
+}
+
+// Waits for a barrier phase; gives up (false) when another warp of the CTA
+// has given up, or after kMbarWaitNs, in which case it raises the CTA's flag.
+__device__ __forceinline__ bool tc_wait(std::uint64_t* bar, unsigned parity, volatile int* abort) {
+    const unsigned long long t0 = global_ns();
+    for (unsigned i = 0; i < kMbarMaxPolls; ++i) {
+        unsigned done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(done)
+            : "r"(smem_addr(bar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 63u) == 63u) {
+            if (*abort) return false;
+            if (global_ns() - t0 > kMbarWaitNs) break;
+        }
+    }
+    *abort = 1;
+    flag_check(B2_CHECK_WAIT);
+    return false;
+}
+
+// Barrier 1 over the 128 softmax threads, returning whether any of them
+// passed `pred`.
+__device__ __forceinline__ bool softmax_group_any(bool pred) {
+    unsigned r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(static_cast<unsigned>(pred)), "n"(kTcSoftmaxThreads)
+        : "memory");
+    return r != 0;
+}
+
+// The trie row of key kp of the chain (none past `last`), as the staging
+// warps and the other kernels read it: out-of-range entries are reported and
+// replaced by an in-range row.
+__device__ __forceinline__ std::uint32_t tc_key_row(const AttnArgs& a, const std::uint32_t* chain, std::size_t kp,
+                                                    std::size_t last, std::size_t n0) {
+    if (kp > last) return 0xFFFFFFFFu;
+    std::uint32_t r = chain[kp];
+    if (r >= a.rows) {
+        flag_check(B2_CHECK_ATTENTION);
+        r = static_cast<std::uint32_t>(n0);
+    }
+    return r;
+}
+
+// x -> (TF32 hi, TF32 lo) of the 3 x TF32 split.
+__device__ __forceinline__ void tc_split(float x, float& hi, float& lo) {
+    hi = tc::tf32_round(x);
+    lo = tc::tf32_round(__fsub_rn(x, hi));
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+attention_tree_tc(AttnArgs a) {
+    pdl_begin();
+    extern __shared__ __align__(16) unsigned char tc_raw[];
+    __shared__ std::uint32_t tmem_base;
+    __shared__ __align__(8) std::uint64_t kfull[kTcKStages], kempty[kTcKStages], vfull[kTcVStages],
+        vempty[kTcVStages], sfull[2], sempty[2], qfull, pfull, ofull;
+    __shared__ int path_s;
+    __shared__ volatile int abort_s;
+    __shared__ std::size_t pos0_s;
+    __shared__ const std::uint32_t* chain_s;
+    // 1024-byte aligned stages (swizzle atoms): keys, values, then O [dim][MMA row]
+    unsigned char* kring = tc_raw + ((1024 - (smem_addr(tc_raw) & 1023u)) & 1023u);
+    unsigned char* vring = kring + kTcKStages * kTcStageBytes;
+    float* oacc = reinterpret_cast<float*>(vring + kTcVStages * kTcStageBytes);
+
+    const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const std::size_t kh = blockIdx.x % a.kv_heads;
+    const std::size_t n0 = (blockIdx.x / a.kv_heads) * kTcRows;
+    const int nr = static_cast<int>(a.rows - n0 < kTcRows ? a.rows - n0 : kTcRows);
+    if (warp == 0) {
+        const std::uint32_t* c;
+        std::size_t p0;
+        const bool path = tc_block_is_path(a, n0, nr, &c, &p0);
+        if (lane == 0) {
+            path_s = path;
+            chain_s = c;
+            pos0_s = p0;
+            abort_s = 0;
+            for (int s = 0; s < kTcKStages; ++s) {
+                mbar_init(&kfull[s], kTcStageThreads);
+                mbar_init(&kempty[s], 1);
+            }
+            for (int s = 0; s < kTcVStages; ++s) {
+                mbar_init(&vfull[s], kTcStageThreads);
+                mbar_init(&vempty[s], 1);
+            }
+            for (int s = 0; s < 2; ++s) {
+                mbar_init(&sfull[s], 1);
+                mbar_init(&sempty[s], kTcSoftmaxThreads);
+            }
+            mbar_init(&qfull, kTcSoftmaxThreads);
+            mbar_init(&pfull, kTcSoftmaxThreads);
+            mbar_init(&ofull, 1);
+        }
+    }
+    __syncthreads();
+    if (!path_s) return;  // attention_tree_block takes this block
+    if (warp == 0) tc::tmem_alloc(&tmem_base, kTcCols);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const std::uint32_t tmem = tmem_base;
+    const std::uint32_t* chain = chain_s;
+    const std::size_t pos0 = pos0_s;
+    const std::size_t last = pos0 + nr - 1;
+    const std::size_t kb0 = pos0 + 1 > a.window ? pos0 + 1 - a.window : 0;
+    const int tiles_n = static_cast<int>((last - kb0 + kTcKeys) / kTcKeys);
+    const std::size_t kv_row = a.kv_heads * 128;
+    constexpr unsigned kSoftmaxWarps = kTcSoftmaxThreads / 32;
+
+    if (warp == kSoftmaxWarps || warp == kSoftmaxWarps + 1) {
+        // ---- key tiles: keys j = w + 2i, lane = float4 of the 128 dims ----
+        const int w = static_cast<int>(warp - kSoftmaxWarps);
+        for (int t = 0; t < tiles_n; ++t) {
+            const int s = t % kTcKStages;
+            if (t >= kTcKStages &&
+                !__all_sync(0xffffffffu, tc_wait(&kempty[s], ((t / kTcKStages) - 1) & 1, &abort_s)))
+                break;
+            unsigned char* hi_t = kring + s * kTcStageBytes;
+            unsigned char* lo_t = hi_t + kTcTileBytes;
+            const std::uint32_t r = tc_key_row(a, chain, kb0 + static_cast<std::size_t>(t) * kTcKeys + lane, last, n0);
+            float4 kv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const std::uint32_t rk = __shfl_sync(0xffffffffu, r, w + 2 * i);
+                kv[i] = rk != 0xFFFFFFFFu
+                            ? ld_plain(reinterpret_cast<const float4*>(a.k + rk * kv_row + kh * 128) + lane)
+                            : zero4();
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                // key j, dims 4 lane .. 4 lane + 3: K-major row j of atom lane / 8, chunk lane % 8
+                const int off = static_cast<int>(lane >> 3) * 4096 + tc::sw128_offset(w + 2 * i, lane & 7);
+                float4 h4, l4;
+                tc_split(kv[i].x, h4.x, l4.x);
+                tc_split(kv[i].y, h4.y, l4.y);
+                tc_split(kv[i].z, h4.z, l4.z);
+                tc_split(kv[i].w, h4.w, l4.w);
+                *reinterpret_cast<float4*>(hi_t + off) = h4;
+                *reinterpret_cast<float4*>(lo_t + off) = l4;
+            }
+            fence_proxy_async_smem();  // the MMAs read the stage through the async proxy
+            mbar_arrive(&kfull[s]);
+        }
+    } else if (warp == kSoftmaxWarps + 2 || warp == kSoftmaxWarps + 3) {
+        // ---- value tiles, transposed: lane = key, float4 c = w + 2i of its dims
+        // (so that the transposed stores hit 32 distinct banks) ----
+        const int w = static_cast<int>(warp - kSoftmaxWarps - 2);
+        for (int t = 0; t < tiles_n; ++t) {
+            const int s = t % kTcVStages;
+            if (t >= kTcVStages &&
+                !__all_sync(0xffffffffu, tc_wait(&vempty[s], ((t / kTcVStages) - 1) & 1, &abort_s)))
+                break;
+            unsigned char* hi_t = vring + s * kTcStageBytes;
+            unsigned char* lo_t = hi_t + kTcTileBytes;
+            const std::uint32_t r = tc_key_row(a, chain, kb0 + static_cast<std::size_t>(t) * kTcKeys + lane, last, n0);
+            float4 vv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                vv[i] = r != 0xFFFFFFFFu
+                            ? ld_plain(reinterpret_cast<const float4*>(a.v + r * kv_row + kh * 128) + w + 2 * i)
+                            : zero4();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                // V^T: row d = 4c + e, K = key lane: chunk lane / 4, element lane % 4
+                const int c = w + 2 * i;
+                const float vx[4] = {vv[i].x, vv[i].y, vv[i].z, vv[i].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int off = tc::sw128_offset(4 * c + e, static_cast<int>(lane >> 2)) +
+                                    static_cast<int>(lane & 3) * 4;
+                    float h, l;
+                    tc_split(vx[e], h, l);
+                    *reinterpret_cast<float*>(hi_t + off) = h;
+                    *reinterpret_cast<float*>(lo_t + off) = l;
+                }
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&vfull[s]);
+        }
+    } else if (warp == kSoftmaxWarps + 4) {
+        // ---- MMA issue (one thread) ----
+        if (lane == 0) {
+            // S(t) = Ql Kh + Qh Kl + Qh Kh into S buffer t % 2
+            auto scores = [&](int t) -> bool {
+                const int s = t % kTcKStages;
+                if (t >= 2 && !tc_wait(&sempty[t & 1], ((t >> 1) - 1) & 1, &abort_s)) return false;
+                if (!tc_wait(&kfull[s], (t / kTcKStages) & 1, &abort_s)) return false;
+                tc::fence_after_sync();
+                constexpr std::uint32_t idesc = tc::tf32_idesc(128, kTcKeys);
+                const unsigned char* k_hi = kring + s * kTcStageBytes;
+                const unsigned char* kb[3] = {k_hi, k_hi + kTcTileBytes, k_hi};
+                const std::uint32_t qa[3] = {kColQl, kColQh, kColQh};
+                const std::uint32_t d = tmem + kColS + 32u * static_cast<std::uint32_t>(t & 1);
+                for (int part = 0; part < 3; ++part)
+                    for (int ks = 0; ks < 16; ++ks)
+                        tc::mma_tf32_ts(d, tmem + qa[part] + ks * 8,
+                                        tc::sw128_desc(kb[part] + (ks >> 2) * 4096 + (ks & 3) * 32), idesc,
+                                        part > 0 || ks > 0);
+                tc::commit(&sfull[t & 1]);
+                if (t + kTcKStages < tiles_n) tc::commit(&kempty[s]);
+                return true;
+            };
+            bool ok = tc_wait(&qfull, 0, &abort_s);
+            ok = ok && scores(0);
+            if (ok && tiles_n > 1) ok = scores(1);
+            for (int t = 0; t < tiles_n && ok; ++t) {
+                if (t + 2 < tiles_n && !scores(t + 2)) break;  // waits until S(t) has been read
+                // P V(t) = Pl Vh + Ph Vl + Ph Vh, once P(t) is in tensor memory
+                const int s = t % kTcVStages;
+                if (!tc_wait(&pfull, t & 1, &abort_s) || !tc_wait(&vfull[s], (t / kTcVStages) & 1, &abort_s)) break;
+                tc::fence_after_sync();
+                constexpr std::uint32_t idesc = tc::tf32_idesc(128, 128);
+                const unsigned char* v_hi = vring + s * kTcStageBytes;
+                const unsigned char* vb[3] = {v_hi, v_hi + kTcTileBytes, v_hi};
+                const std::uint32_t pa[3] = {kColPl, kColPh, kColPh};
+                for (int part = 0; part < 3; ++part)
+                    for (int ks = 0; ks < kTcKeys / 8; ++ks)
+                        tc::mma_tf32_ts(tmem + kColO, tmem + pa[part] + ks * 8, tc::sw128_desc(vb[part] + ks * 32),
+                                        idesc, part > 0 || ks > 0);
+                tc::commit(&ofull);
+                if (t + kTcVStages < tiles_n) tc::commit(&vempty[s]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---- softmax warps ----
+        const std::uint32_t lane_base = static_cast<std::uint32_t>(warp * 32) << 16;
+        const int ri = static_cast<int>(tid >> 2), hg = static_cast<int>(tid & 3);  // this thread's row and head
+        const bool row_ok = ri < nr;
+        const std::size_t pos_i = pos0 + ri;
+        // Q hi / lo into tensor memory (lane tid, 128 columns each); O = 0
+        {
+            const float* qr = a.q + ((n0 + (row_ok ? ri : 0)) * a.q_heads + kh * kGroup + hg) * 128;
+            for (int c0 = 0; c0 < 128; c0 += 32) {
+                float hi[32], lo[32];
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const float4 v = row_ok ? ld_plain(reinterpret_cast<const float4*>(qr + c0 + j)) : zero4();
+                    tc_split(v.x, hi[j], lo[j]);
+                    tc_split(v.y, hi[j + 1], lo[j + 1]);
+                    tc_split(v.z, hi[j + 2], lo[j + 2]);
+                    tc_split(v.w, hi[j + 3], lo[j + 3]);
+                }
+                tc::st32(tmem + lane_base + kColQh + c0, hi);
+                tc::st32(tmem + lane_base + kColQl + c0, lo);
+            }
+            tc::st_wait();
+            tc::fence_before_sync();
+            mbar_arrive(&qfull);
+            for (int c = 0; c < 128; ++c) oacc[c * kTcSoftmaxThreads + tid] = 0.0f;
+        }
+        // folds the P V of the tile issued last into O: O = O * alpha + PV
+        auto fold = [&](float alpha) {
+            for (int c0 = 0; c0 < 128; c0 += 32) {
+                float o[32];
+                tc::ld32(tmem + lane_base + kColO + c0, o);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    float* dst = oacc + (c0 + j) * kTcSoftmaxThreads + tid;
+                    *dst = __fmaf_rn(*dst, alpha, o[j]);
+                }
+            }
+        };
+        const float scale = a.scale;
+        float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
+        bool ok = true;
+        for (int t = 0; t < tiles_n && ok; ++t) {
+            ok = __all_sync(0xffffffffu, tc_wait(&sfull[t & 1], (t >> 1) & 1, &abort_s));
+            if (!ok) break;
+            tc::fence_after_sync();
+            float ph[32], pl[32];
+            tc::ld32(tmem + lane_base + kColS + 32u * static_cast<std::uint32_t>(t & 1), ph);
+            tc::fence_before_sync();
+            mbar_arrive(&sempty[t & 1]);  // S(t + 2) may be computed into this buffer
+            const std::size_t kt = kb0 + static_cast<std::size_t>(t) * kTcKeys;
+            float mt = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const std::size_t kp = kt + j;
+                const bool valid = row_ok && kp <= pos_i && kp + a.window > pos_i;
+                ph[j] = valid ? __fmul_rn(ph[j], scale) : -INFINITY;
+                mt = fmaxf(mt, ph[j]);
+            }
+            const float mn = fmaxf(m, mt);
+            float alpha = 1.0f;
+            if (mn != -INFINITY && mn != m) alpha = expf(__fsub_rn(m, mn));  // 0 while m is -inf
+            l = __fmul_rn(l, alpha);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float p = ph[j] == -INFINITY ? 0.0f : expf(__fsub_rn(ph[j], mn));
+                l = __fadd_rn(l, p);
+                tc_split(p, ph[j], pl[j]);
+            }
+            m = mn;
+            if (t > 0) {  // P V(t - 1) done: fold it, and P's columns are free
+                ok = __all_sync(0xffffffffu, tc_wait(&ofull, (t - 1) & 1, &abort_s));
+                if (!ok) break;
+                tc::fence_after_sync();
+                fold(alpha_prev);
+            }
+            alpha_prev = alpha;
+            tc::st32(tmem + lane_base + kColPh, ph);
+            tc::st32(tmem + lane_base + kColPl, pl);
+            tc::st_wait();
+            tc::fence_before_sync();
+            mbar_arrive(&pfull);  // also: this thread's reads of the P V columns are done
+        }
+        if (ok) {
+            ok = __all_sync(0xffffffffu, tc_wait(&ofull, (tiles_n - 1) & 1, &abort_s));
+            if (ok) {
+                tc::fence_after_sync();
+                fold(alpha_prev);
+            }
+        }
+        // ---- epilogue: out = O / l ----
+        if (!softmax_group_any(!ok) && row_ok) {
+            const float inv = __fdiv_rn(1.0f, l);
+            float* orow = a.out + ((n0 + ri) * a.q_heads + kh * kGroup + hg) * 128;
+            for (int c = 0; c < 128; c += 4)
+                st_plain(reinterpret_cast<float4*>(orow + c),
+                         make_float4(__fmul_rn(oacc[c * kTcSoftmaxThreads + tid], inv),
+                                     __fmul_rn(oacc[(c + 1) * kTcSoftmaxThreads + tid], inv),
+                                     __fmul_rn(oacc[(c + 2) * kTcSoftmaxThreads + tid], inv),
+                                     __fmul_rn(oacc[(c + 3) * kTcSoftmaxThreads + tid], inv)));
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_free(tmem, kTcCols);
 }
 
 // ---- query-blocked kernel (head_dim 128) --------------------------------------
@@ -565,6 +974,19 @@ attention_tree_block(AttnArgs a, std::size_t wcap) {
     const std::size_t kh = blockIdx.x % a.kv_heads;
     const std::size_t n0 = (blockIdx.x / a.kv_heads) * kBlkRows;
     const int nrows = static_cast<int>(a.rows - n0 < kBlkRows ? a.rows - n0 : kBlkRows);
+    if (!EXACT && a.tc_paths) {  // rows of a 32-row path block: attention_tree_tc wrote them
+        __shared__ int done_s;
+        if (threadIdx.x < 32) {
+            const std::size_t t0 = n0 / kTcRows * kTcRows;
+            const int tn = static_cast<int>(a.rows - t0 < kTcRows ? a.rows - t0 : kTcRows);
+            const std::uint32_t* c;
+            std::size_t p0;
+            const bool path = tc_block_is_path(a, t0, tn, &c, &p0);
+            if (threadIdx.x == 0) done_s = path;
+        }
+        __syncthreads();
+        if (done_s) return;
+    }
     if (threadIdx.x == 0) {
         // segments: maximal runs in which row n is the child of row n - 1
         int nseg = 0;
@@ -647,6 +1069,15 @@ int attention_launch(AttnArgs& a, std::size_t head_dim, std::uint32_t flags, b2_
         auto kernel = exact ? attention_tree_block<true> : attention_tree_block<false>;
         if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
             return launch_result("b2_attention_tree: shared memory attribute");
+        if (!exact && (rows + kTcRows - 1) / kTcRows * kv_heads <= 0x7FFFFFFFu) {
+            // tree order: the path blocks on the tensor cores first; the block
+            // kernel below then takes only the rows of the other blocks
+            if (allow_dynamic_smem(reinterpret_cast<const void*>(attention_tree_tc), kTcSmem) != cudaSuccess)
+                return launch_result("b2_attention_tree: shared memory attribute");
+            launch_pdl(attention_tree_tc, static_cast<unsigned>((rows + kTcRows - 1) / kTcRows * kv_heads), kTcThreads,
+                       kTcSmem, s, a);
+            a.tc_paths = 1;
+        }
         launch_pdl(kernel, static_cast<unsigned>((rows + kBlkRows - 1) / kBlkRows * kv_heads), kBlkThreads, smem,
                    s, a, wcap);
         return launch_result("b2_attention_tree");
