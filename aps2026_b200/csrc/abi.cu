@@ -13,7 +13,19 @@ thread_local std::string t_last_error;
 
 struct DeviceInfo {
     int sms = 0;
+    cudaMemPool_t scratch = nullptr;  // scratch_alloc's pool on this device
 };
+
+cudaError_t make_scratch_pool(int dev, cudaMemPool_t* pool) {
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaError_t e = cudaMemPoolCreate(pool, &props);
+    if (e != cudaSuccess) return e;
+    std::uint64_t keep = ~std::uint64_t(0);  // never trim at synchronisation points
+    return cudaMemPoolSetAttribute(*pool, cudaMemPoolAttrReleaseThreshold, &keep);
+}
 std::mutex g_info_mutex;
 std::vector<DeviceInfo> g_info;
 }  // namespace
@@ -36,6 +48,32 @@ int sm_count() {
         info.sms = n;
     }
     return info.sms;
+}
+
+cudaError_t scratch_alloc(void** p, std::size_t bytes, cudaStream_t stream) {
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess) {
+        cudaGetLastError();
+        capture = cudaStreamCaptureStatusNone;
+    }
+    if (capture != cudaStreamCaptureStatusNone) return cudaMallocAsync(p, bytes, stream);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(g_info_mutex);
+    if (static_cast<std::size_t>(dev) >= g_info.size()) g_info.resize(dev + 1);
+    DeviceInfo& info = g_info[dev];
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        if (!info.scratch && (e = make_scratch_pool(dev, &info.scratch)) != cudaSuccess) {
+            info.scratch = nullptr;
+            return e;
+        }
+        e = cudaMallocFromPoolAsync(p, bytes, info.scratch, stream);
+        if (e == cudaSuccess || e == cudaErrorMemoryAllocation) return e;
+        cudaGetLastError();  // a pool of an earlier context (device reset): make a new one
+        info.scratch = nullptr;
+    }
+    return e;
 }
 
 int resident_ctas(const void* kernel, int threads, std::size_t smem) {

@@ -54,6 +54,10 @@ struct AttnArgs {
     const std::uint32_t* token_node;   // [total]
     std::size_t prompts, total;
     int tc_paths;                      // attention_tree_tc ran: path blocks of 32 rows are done
+    // with tc_paths: the count and list of the (32-row block, KV head) pairs
+    // attention_tree_tc left to attention_tree_block
+    const std::uint32_t* tc_rest_count;
+    const std::uint32_t* tc_rest;
 };
 
 // First key of the ancestor chain of row n at position pos (its keys are
@@ -257,43 +261,68 @@ attention_tree_kernel(AttnArgs a) {
 // is lo.hi + hi.lo + hi.hi -- three kind::tf32 MMAs into one FP32
 // accumulator in tensor memory (relative error ~2^-22 per product).
 //
-// One CTA per (block of 32 consecutive trie rows that form a path, KV head):
-// M = 32 rows x 4 query heads = 128 rows of the MMA, and the keys of every
-// row are a prefix of the deepest row's chain, so each 32-key tile of that
-// chain is staged once for all 128 rows.
+// tc_split_kv writes the hi / lo planes of K and V once per call. One CTA of
+// attention_tree_tc per (block of 32 consecutive trie rows that form a path,
+// KV head): M = 32 rows x 4 query heads = 128 rows of the MMA, and the keys
+// of every row are a prefix of the deepest row's chain, so each 32-key tile
+// of that chain is staged once for all 128 rows.
 //   tensor memory  Q hi / lo [128 x 128] (the A operand of S = Q K^T), S
 //                  [128 x 32] twice, P hi / lo [128 x 32] (the A operand of
 //                  P V), the tile's P V [128 x 128];
-//   shared memory  a ring of 3 key tiles hi / lo [32 keys x 128 dims] and a
-//                  ring of 2 value tiles transposed, hi / lo [128 dims x 32
-//                  keys], K-major in the 128-byte swizzle layout; O [128
-//                  dims][128 MMA rows].
-// Warp roles: 4-5 stage key tiles, 6-7 value tiles (global loads, the
-// split, swizzled stores); 8 issues the MMAs -- S(t + 2) as soon as S(t) has
-// been read, P V(t) once P(t) is written; 0-3 own one MMA row each (thread
-// m: row m / 4 of the block, query head m % 4 of the group, tensor-memory
-// lane m) and run the softmax online: per tile, the row's running maximum m
-// and sum l are updated (l = l * exp(m_old - m) + sum p, p = expf(s * scale
-// - m), 0 outside the row's window), and the previous tile's P V is folded
-// into O as O = O * exp(m_old - m) + PV in FP32 round-to-nearest (the
-// tensor core's accumulator truncates; chaining every tile there biased long
-// windows by ~1e-6). The epilogue writes O * (1 / l): the softmax of the
-// tree-order SIMT kernel, formed in another order. Blocks that are not a
-// path (prompt boundaries, shared-prefix branch points) are left to
-// attention_tree_block, which skips the path blocks by the same test.
+//   shared memory  a ring of 3 key tiles hi / lo [32 keys x 128 dims]
+//                  (K-major, 128-byte swizzle) and a ring of 2 value tiles
+//                  hi / lo [32 keys x 128 dims] (the B operand of P V with
+//                  its N = dims contiguous: MN-major, 128-byte rows with
+//                  32-byte swizzle granules); O [128 dims / 4][128 MMA rows]
+//                  float4s.
+// Warp roles: 4 stages key tiles, 5 value tiles (16-byte cp.async copies
+// of the planes into the swizzled layouts); 6 issues the MMAs -- S(t + 2)
+// as soon as S(t) has been read, P V(t) once P(t) is written; 0-3 own one
+// MMA row each (thread m: row m / 4 of the block, query head m % 4 of the
+// group, tensor-memory lane m) and run the softmax online in base 2: with
+// s2 = s * scale * log2(e) per key, the row's running maximum m and sum l
+// are updated per tile (l = l * 2^(m_old - m) + sum p, p = 2^(s2 - m), 0
+// outside the row's window), and the previous tile's P V is folded into O
+// as O = O * 2^(m_old - m) + PV in FP32 round-to-nearest (the tensor core's
+// accumulator truncates; chaining every tile there biased long windows by
+// ~1e-6). The epilogue writes O * (1 / l): the softmax of the tree-order
+// SIMT kernel, formed in another order. Blocks that are not a path (prompt
+// boundaries, shared-prefix branch points) are left to attention_tree_block,
+// which skips the path blocks by the same test.
 constexpr int kTcRows = 32;  // trie rows per CTA (x 4 heads = M 128)
 constexpr int kTcKeys = 32;  // chain keys per tile
 constexpr int kTcSoftmaxThreads = 128;                      // warps 0-3
-constexpr int kTcStageThreads = 64;                         // warps 4-5 (keys), 6-7 (values)
-constexpr int kTcThreads = kTcSoftmaxThreads + 2 * kTcStageThreads + 32;  // + warp 8 (MMA)
+constexpr int kTcThreads = kTcSoftmaxThreads + 3 * 32;      // + key, value and MMA warps
 constexpr int kTcKStages = 3, kTcVStages = 2;
 constexpr std::uint32_t kColQh = 0, kColQl = 128, kColO = 256, kColS = 384, kColPh = 448, kColPl = 480;
 constexpr std::uint32_t kTcCols = 512;
-constexpr int kTcTileBytes = 16 * 1024;  // one operand tile: 32 x 128 or 128 x 32 fp32
+constexpr int kTcTileBytes = 16 * 1024;  // one operand tile: 32 x 128 fp32
 constexpr int kTcStageBytes = 2 * kTcTileBytes;  // hi, lo
 // rings + O + 1024-byte alignment (225 KB: one CTA per SM, each allocating
 // all 512 tensor-memory columns)
 constexpr std::size_t kTcSmem = (kTcKStages + kTcVStages) * kTcStageBytes + 128 * 128 * 4 + 1024;
+
+// Byte offset of dims 4c .. 4c + 3 of key j in a key tile: K-major rows of
+// 128 bytes (32 dims), 8-key atoms of 1024 bytes, the four 32-dim blocks
+// 4096 bytes apart, 16-byte chunks swizzled by j % 8.
+__device__ __forceinline__ int tc_key_offset(int j, int c) { return (c >> 3) * 4096 + tc::sw128_offset(j, c & 7); }
+// ... in a value tile: rows of 128 bytes (32 dims) per key, 4-key groups of
+// 512 bytes, the four 32-dim blocks 4096 bytes apart, 32-byte granules
+// swizzled by j % 4 (the MN-major SWIZZLE_128B_BASE32B layout).
+__device__ __forceinline__ int tc_value_offset(int j, int c) {
+    return (c >> 3) * 4096 + (j >> 2) * 512 + (j & 3) * 128 + ((((c >> 1) & 3) ^ (j & 3)) << 5) + (c & 1) * 16;
+}
+// P V's B descriptor at key group ks (8 keys = two 4-key groups): MN-major,
+// 32-dim blocks 4096 bytes apart (leading byte offset), 4-key groups 512
+// bytes apart (stride byte offset).
+__device__ __forceinline__ std::uint64_t tc_value_desc(const void* p) {
+    std::uint64_t d = static_cast<std::uint64_t>((smem_addr(p) >> 4) & 0x3FFFu);
+    d |= static_cast<std::uint64_t>(4096 >> 4) << 16;
+    d |= static_cast<std::uint64_t>(512 >> 4) << 32;
+    d |= static_cast<std::uint64_t>(1) << 46;  // descriptor version (sm_100)
+    d |= static_cast<std::uint64_t>(1) << 61;  // layout: 128-byte swizzle, 32-byte base
+    return d;
+}
 
 // Whether rows n0 .. n0 + nr - 1 form a path whose chains are prefixes of the
 // last row's chain: consecutive positions, each row found in the last row's
@@ -351,9 +380,8 @@ __device__ __forceinline__ bool softmax_group_any(bool pred) {
     return r != 0;
 }
 
-// The trie row of key kp of the chain (none past `last`), as the staging
-// warps and the other kernels read it: out-of-range entries are reported and
-// replaced by an in-range row.
+// The trie row of key kp of the chain (none past `last`); out-of-range
+// entries are reported and replaced by an in-range row.
 __device__ __forceinline__ std::uint32_t tc_key_row(const AttnArgs& a, const std::uint32_t* chain, std::size_t kp,
                                                     std::size_t last, std::size_t n0) {
     if (kp > last) return 0xFFFFFFFFu;
@@ -371,8 +399,46 @@ __device__ __forceinline__ void tc_split(float x, float& hi, float& lo) {
     lo = tc::tf32_round(__fsub_rn(x, hi));
 }
 
+// 2^x (ex2.approx: relative error ~2^-22; 2^-inf = 0).
+__device__ __forceinline__ float tc_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 16-byte copy global -> shared (L2 only), zero-filled when !valid.
+__device__ __forceinline__ void tc_copy16(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+                 "r"(valid ? 16u : 0u)
+                 : "memory");
+}
+
+// K and V -> hi / lo planes: split[0..3] = K hi, K lo, V hi, V lo, each
+// [rows][kv_heads * 128]; zeroes the count of blocks attention_tree_tc leaves.
+__global__ void __launch_bounds__(256) tc_split_kv(const float4* k, const float4* v, float4* split,
+                                                   std::size_t n4, std::uint32_t* rest_count) {
+    pdl_begin();
+    if (blockIdx.x == 0 && threadIdx.x == 0) *rest_count = 0;
+    for (std::size_t i = blockIdx.x * std::size_t(256) + threadIdx.x; i < n4; i += std::size_t(gridDim.x) * 256) {
+        const float4 kx = ld_plain(k + i), vx = ld_plain(v + i);
+        float4 h, l;
+        tc_split(kx.x, h.x, l.x);
+        tc_split(kx.y, h.y, l.y);
+        tc_split(kx.z, h.z, l.z);
+        tc_split(kx.w, h.w, l.w);
+        split[i] = h;
+        split[n4 + i] = l;
+        tc_split(vx.x, h.x, l.x);
+        tc_split(vx.y, h.y, l.y);
+        tc_split(vx.z, h.z, l.z);
+        tc_split(vx.w, h.w, l.w);
+        split[2 * n4 + i] = h;
+        split[3 * n4 + i] = l;
+    }
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
-attention_tree_tc(AttnArgs a) {
+attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std::uint32_t* rest) {
     pdl_begin();
     extern __shared__ __align__(16) unsigned char tc_raw[];
     __shared__ std::uint32_t tmem_base;
@@ -382,10 +448,10 @@ attention_tree_tc(AttnArgs a) {
     __shared__ volatile int abort_s;
     __shared__ std::size_t pos0_s;
     __shared__ const std::uint32_t* chain_s;
-    // 1024-byte aligned stages (swizzle atoms): keys, values, then O [dim][MMA row]
+    // 1024-byte aligned stages (swizzle atoms): keys, values, then O
     unsigned char* kring = tc_raw + ((1024 - (smem_addr(tc_raw) & 1023u)) & 1023u);
     unsigned char* vring = kring + kTcKStages * kTcStageBytes;
-    float* oacc = reinterpret_cast<float*>(vring + kTcVStages * kTcStageBytes);
+    float4* oacc = reinterpret_cast<float4*>(vring + kTcVStages * kTcStageBytes);
 
     const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const std::size_t kh = blockIdx.x % a.kv_heads;
@@ -401,11 +467,11 @@ attention_tree_tc(AttnArgs a) {
             pos0_s = p0;
             abort_s = 0;
             for (int s = 0; s < kTcKStages; ++s) {
-                mbar_init(&kfull[s], kTcStageThreads);
+                mbar_init(&kfull[s], 32);
                 mbar_init(&kempty[s], 1);
             }
             for (int s = 0; s < kTcVStages; ++s) {
-                mbar_init(&vfull[s], kTcStageThreads);
+                mbar_init(&vfull[s], 32);
                 mbar_init(&vempty[s], 1);
             }
             for (int s = 0; s < 2; ++s) {
@@ -418,7 +484,10 @@ attention_tree_tc(AttnArgs a) {
         }
     }
     __syncthreads();
-    if (!path_s) return;  // attention_tree_block takes this block
+    if (!path_s) {  // attention_tree_block takes this block
+        if (tid == 0) rest[atomicAdd(rest_count, 1u)] = blockIdx.x;
+        return;
+    }
     if (warp == 0) tc::tmem_alloc(&tmem_base, kTcCols);
     tc::fence_before_sync();
     __syncthreads();
@@ -433,76 +502,39 @@ attention_tree_tc(AttnArgs a) {
     constexpr unsigned kSoftmaxWarps = kTcSoftmaxThreads / 32;
 
     if (warp == kSoftmaxWarps || warp == kSoftmaxWarps + 1) {
-        // ---- key tiles: keys j = w + 2i, lane = float4 of the 128 dims ----
-        const int w = static_cast<int>(warp - kSoftmaxWarps);
+        // ---- staging: warp 4 the key tiles into a ring of 3, warp 5 the value
+        // tiles into a ring of 2; lane = 16-byte chunk c of a key's 128 dims.
+        // Each lane's copies of a tile arrive on the stage's barrier when they
+        // have landed (cp.async.mbarrier.arrive.noinc: one of its 32
+        // arrivals). ----
+        const bool keys = warp == kSoftmaxWarps;
+        const int stages = keys ? kTcKStages : kTcVStages;
+        unsigned char* ring = keys ? kring : vring;
+        std::uint64_t* full = keys ? kfull : vfull;
+        std::uint64_t* empty = keys ? kempty : vempty;
+        const std::size_t plane = a.rows * kv_row;
+        const float* hi_p = split + (keys ? 0 : 2 * plane) + kh * 128 + 4 * lane;
+        const float* lo_p = hi_p + plane;
         for (int t = 0; t < tiles_n; ++t) {
-            const int s = t % kTcKStages;
-            if (t >= kTcKStages &&
-                !__all_sync(0xffffffffu, tc_wait(&kempty[s], ((t / kTcKStages) - 1) & 1, &abort_s)))
+            const int s = t % stages;
+            if (t >= stages && !__all_sync(0xffffffffu, tc_wait(&empty[s], ((t / stages) - 1) & 1, &abort_s)))
                 break;
-            unsigned char* hi_t = kring + s * kTcStageBytes;
+            unsigned char* hi_t = ring + s * kTcStageBytes;
             unsigned char* lo_t = hi_t + kTcTileBytes;
             const std::uint32_t r = tc_key_row(a, chain, kb0 + static_cast<std::size_t>(t) * kTcKeys + lane, last, n0);
-            float4 kv[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const std::uint32_t rk = __shfl_sync(0xffffffffu, r, w + 2 * i);
-                kv[i] = rk != 0xFFFFFFFFu
-                            ? ld_plain(reinterpret_cast<const float4*>(a.k + rk * kv_row + kh * 128) + lane)
-                            : zero4();
+#pragma unroll 8
+            for (int j = 0; j < kTcKeys; ++j) {
+                const std::uint32_t rk = __shfl_sync(0xffffffffu, r, j);
+                const bool valid = rk != 0xFFFFFFFFu;
+                const std::size_t src = valid ? rk * kv_row : 0;
+                const int off = keys ? tc_key_offset(j, static_cast<int>(lane)) : tc_value_offset(j, static_cast<int>(lane));
+                tc_copy16(hi_t + off, hi_p + src, valid);
+                tc_copy16(lo_t + off, lo_p + src, valid);
             }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                // key j, dims 4 lane .. 4 lane + 3: K-major row j of atom lane / 8, chunk lane % 8
-                const int off = static_cast<int>(lane >> 3) * 4096 + tc::sw128_offset(w + 2 * i, lane & 7);
-                float4 h4, l4;
-                tc_split(kv[i].x, h4.x, l4.x);
-                tc_split(kv[i].y, h4.y, l4.y);
-                tc_split(kv[i].z, h4.z, l4.z);
-                tc_split(kv[i].w, h4.w, l4.w);
-                *reinterpret_cast<float4*>(hi_t + off) = h4;
-                *reinterpret_cast<float4*>(lo_t + off) = l4;
-            }
-            fence_proxy_async_smem();  // the MMAs read the stage through the async proxy
-            mbar_arrive(&kfull[s]);
+            asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(&full[s])) : "memory");
         }
-    } else if (warp == kSoftmaxWarps + 2 || warp == kSoftmaxWarps + 3) {
-        // ---- value tiles, transposed: lane = key, float4 c = w + 2i of its dims
-        // (so that the transposed stores hit 32 distinct banks) ----
-        const int w = static_cast<int>(warp - kSoftmaxWarps - 2);
-        for (int t = 0; t < tiles_n; ++t) {
-            const int s = t % kTcVStages;
-            if (t >= kTcVStages &&
-                !__all_sync(0xffffffffu, tc_wait(&vempty[s], ((t / kTcVStages) - 1) & 1, &abort_s)))
-                break;
-            unsigned char* hi_t = vring + s * kTcStageBytes;
-            unsigned char* lo_t = hi_t + kTcTileBytes;
-            const std::uint32_t r = tc_key_row(a, chain, kb0 + static_cast<std::size_t>(t) * kTcKeys + lane, last, n0);
-            float4 vv[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-                vv[i] = r != 0xFFFFFFFFu
-                            ? ld_plain(reinterpret_cast<const float4*>(a.v + r * kv_row + kh * 128) + w + 2 * i)
-                            : zero4();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                // V^T: row d = 4c + e, K = key lane: chunk lane / 4, element lane % 4
-                const int c = w + 2 * i;
-                const float vx[4] = {vv[i].x, vv[i].y, vv[i].z, vv[i].w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int off = tc::sw128_offset(4 * c + e, static_cast<int>(lane >> 2)) +
-                                    static_cast<int>(lane & 3) * 4;
-                    float h, l;
-                    tc_split(vx[e], h, l);
-                    *reinterpret_cast<float*>(hi_t + off) = h;
-                    *reinterpret_cast<float*>(lo_t + off) = l;
-                }
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(&vfull[s]);
-        }
-    } else if (warp == kSoftmaxWarps + 4) {
+        asm volatile("cp.async.wait_all;" ::: "memory");  // none in flight when the CTA ends
+    } else if (warp == kSoftmaxWarps + 2) {
         // ---- MMA issue (one thread) ----
         if (lane == 0) {
             // S(t) = Ql Kh + Qh Kl + Qh Kh into S buffer t % 2
@@ -530,17 +562,17 @@ attention_tree_tc(AttnArgs a) {
             if (ok && tiles_n > 1) ok = scores(1);
             for (int t = 0; t < tiles_n && ok; ++t) {
                 if (t + 2 < tiles_n && !scores(t + 2)) break;  // waits until S(t) has been read
-                // P V(t) = Pl Vh + Ph Vl + Ph Vh, once P(t) is in tensor memory
+                // P V(t) = Pl Vh + Ph Vl + Ph Vh (B = V MN-major), once P(t) is in tensor memory
                 const int s = t % kTcVStages;
                 if (!tc_wait(&pfull, t & 1, &abort_s) || !tc_wait(&vfull[s], (t / kTcVStages) & 1, &abort_s)) break;
                 tc::fence_after_sync();
-                constexpr std::uint32_t idesc = tc::tf32_idesc(128, 128);
+                constexpr std::uint32_t idesc = tc::tf32_idesc(128, 128) | (1u << 16);
                 const unsigned char* v_hi = vring + s * kTcStageBytes;
                 const unsigned char* vb[3] = {v_hi, v_hi + kTcTileBytes, v_hi};
                 const std::uint32_t pa[3] = {kColPl, kColPh, kColPh};
                 for (int part = 0; part < 3; ++part)
                     for (int ks = 0; ks < kTcKeys / 8; ++ks)
-                        tc::mma_tf32_ts(tmem + kColO, tmem + pa[part] + ks * 8, tc::sw128_desc(vb[part] + ks * 32),
+                        tc::mma_tf32_ts(tmem + kColO, tmem + pa[part] + ks * 8, tc_value_desc(vb[part] + ks * 1024),
                                         idesc, part > 0 || ks > 0);
                 tc::commit(&ofull);
                 if (t + kTcVStages < tiles_n) tc::commit(&vempty[s]);
@@ -572,7 +604,7 @@ attention_tree_tc(AttnArgs a) {
             tc::st_wait();
             tc::fence_before_sync();
             mbar_arrive(&qfull);
-            for (int c = 0; c < 128; ++c) oacc[c * kTcSoftmaxThreads + tid] = 0.0f;
+            for (int c = 0; c < 32; ++c) oacc[c * kTcSoftmaxThreads + tid] = zero4();
         }
         // folds the P V of the tile issued last into O: O = O * alpha + PV
         auto fold = [&](float alpha) {
@@ -580,13 +612,23 @@ attention_tree_tc(AttnArgs a) {
                 float o[32];
                 tc::ld32(tmem + lane_base + kColO + c0, o);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    float* dst = oacc + (c0 + j) * kTcSoftmaxThreads + tid;
-                    *dst = __fmaf_rn(*dst, alpha, o[j]);
+                for (int q = 0; q < 8; ++q) {
+                    float4* dst = oacc + ((c0 >> 2) + q) * kTcSoftmaxThreads + tid;
+                    float4 x = *dst;
+                    x.x = __fmaf_rn(x.x, alpha, o[4 * q]);
+                    x.y = __fmaf_rn(x.y, alpha, o[4 * q + 1]);
+                    x.z = __fmaf_rn(x.z, alpha, o[4 * q + 2]);
+                    x.w = __fmaf_rn(x.w, alpha, o[4 * q + 3]);
+                    *dst = x;
                 }
             }
         };
-        const float scale = a.scale;
+        const float scale2 = __fmul_rn(a.scale, 1.4426950408889634f);  // scale * log2(e)
+        // the keys kb0 + lo_k .. kb0 + hi_k are in this row's window
+        const long long lo_k = row_ok ? static_cast<long long>(pos_i + 1 > a.window ? pos_i + 1 - a.window : 0) -
+                                            static_cast<long long>(kb0)
+                                      : 1;
+        const long long hi_k = row_ok ? static_cast<long long>(pos_i - kb0) : 0;
         float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
         bool ok = true;
         for (int t = 0; t < tiles_n && ok; ++t) {
@@ -597,25 +639,30 @@ attention_tree_tc(AttnArgs a) {
             tc::ld32(tmem + lane_base + kColS + 32u * static_cast<std::uint32_t>(t & 1), ph);
             tc::fence_before_sync();
             mbar_arrive(&sempty[t & 1]);  // S(t + 2) may be computed into this buffer
-            const std::size_t kt = kb0 + static_cast<std::size_t>(t) * kTcKeys;
+            // window of this row within the tile: j in [jlo, jhi]
+            const long long t0 = static_cast<long long>(t) * kTcKeys;
+            const int jlo = static_cast<int>(lo_k - t0 < 0 ? 0 : (lo_k - t0 > 32 ? 32 : lo_k - t0));
+            const int jhi = static_cast<int>(hi_k - t0 > 31 ? 31 : (hi_k - t0 < -1 ? -1 : hi_k - t0));
             float mt = -INFINITY;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-                const std::size_t kp = kt + j;
-                const bool valid = row_ok && kp <= pos_i && kp + a.window > pos_i;
-                ph[j] = valid ? __fmul_rn(ph[j], scale) : -INFINITY;
+                ph[j] = (j >= jlo && j <= jhi) ? __fmul_rn(ph[j], scale2) : -INFINITY;
                 mt = fmaxf(mt, ph[j]);
             }
             const float mn = fmaxf(m, mt);
-            float alpha = 1.0f;
-            if (mn != -INFINITY && mn != m) alpha = expf(__fsub_rn(m, mn));  // 0 while m is -inf
-            l = __fmul_rn(l, alpha);
+            const float mref = mn == -INFINITY ? 0.0f : mn;
+            const float alpha = tc_exp2(__fsub_rn(m, mref));  // 0 while m is -inf, 1 while it holds
+            float l0 = 0.0f, l1 = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float p = ph[j] == -INFINITY ? 0.0f : expf(__fsub_rn(ph[j], mn));
-                l = __fadd_rn(l, p);
-                tc_split(p, ph[j], pl[j]);
+            for (int j = 0; j < 32; j += 2) {
+                const float p0 = tc_exp2(__fsub_rn(ph[j], mref));
+                const float p1 = tc_exp2(__fsub_rn(ph[j + 1], mref));
+                l0 = __fadd_rn(l0, p0);
+                l1 = __fadd_rn(l1, p1);
+                tc_split(p0, ph[j], pl[j]);
+                tc_split(p1, ph[j + 1], pl[j + 1]);
             }
+            l = __fmaf_rn(l, alpha, __fadd_rn(l0, l1));
             m = mn;
             if (t > 0) {  // P V(t - 1) done: fold it, and P's columns are free
                 ok = __all_sync(0xffffffffu, tc_wait(&ofull, (t - 1) & 1, &abort_s));
@@ -640,13 +687,12 @@ attention_tree_tc(AttnArgs a) {
         // ---- epilogue: out = O / l ----
         if (!softmax_group_any(!ok) && row_ok) {
             const float inv = __fdiv_rn(1.0f, l);
-            float* orow = a.out + ((n0 + ri) * a.q_heads + kh * kGroup + hg) * 128;
-            for (int c = 0; c < 128; c += 4)
-                st_plain(reinterpret_cast<float4*>(orow + c),
-                         make_float4(__fmul_rn(oacc[c * kTcSoftmaxThreads + tid], inv),
-                                     __fmul_rn(oacc[(c + 1) * kTcSoftmaxThreads + tid], inv),
-                                     __fmul_rn(oacc[(c + 2) * kTcSoftmaxThreads + tid], inv),
-                                     __fmul_rn(oacc[(c + 3) * kTcSoftmaxThreads + tid], inv)));
+            float4* orow = reinterpret_cast<float4*>(a.out + ((n0 + ri) * a.q_heads + kh * kGroup + hg) * 128);
+            for (int c = 0; c < 32; ++c) {
+                const float4 x = oacc[c * kTcSoftmaxThreads + tid];
+                st_plain(orow + c, make_float4(__fmul_rn(x.x, inv), __fmul_rn(x.y, inv), __fmul_rn(x.z, inv),
+                                               __fmul_rn(x.w, inv)));
+            }
         }
     }
     tc::fence_before_sync();
@@ -971,57 +1017,62 @@ attention_tree_block(AttnArgs a, std::size_t wcap) {
     __shared__ int seg_s[kBlkRows + 1], bad_s[kBlkRows], nseg_s;
     __shared__ float red_s[(kBlkThreads / 32) * kCombos];
     load_exp2_table(tab);
-    const std::size_t kh = blockIdx.x % a.kv_heads;
-    const std::size_t n0 = (blockIdx.x / a.kv_heads) * kBlkRows;
-    const int nrows = static_cast<int>(a.rows - n0 < kBlkRows ? a.rows - n0 : kBlkRows);
-    if (!EXACT && a.tc_paths) {  // rows of a 32-row path block: attention_tree_tc wrote them
-        __shared__ int done_s;
-        if (threadIdx.x < 32) {
-            const std::size_t t0 = n0 / kTcRows * kTcRows;
-            const int tn = static_cast<int>(a.rows - t0 < kTcRows ? a.rows - t0 : kTcRows);
-            const std::uint32_t* c;
-            std::size_t p0;
-            const bool path = tc_block_is_path(a, t0, tn, &c, &p0);
-            if (threadIdx.x == 0) done_s = path;
+    // Alone, CTA i takes the kBlkRows rows of block i / kv_heads and KV head
+    // i % kv_heads. After attention_tree_tc (tc_paths), the CTAs stride over
+    // the blocks of kBlkRows rows inside the (32-row block, KV head) pairs it
+    // left, listed in tc_rest.
+    constexpr std::size_t kSub = kTcRows / kBlkRows;
+    const std::size_t units = (!EXACT && a.tc_paths) ? std::size_t(*a.tc_rest_count) * kSub : gridDim.x;
+    const std::size_t stride = (!EXACT && a.tc_paths) ? gridDim.x : units;
+    for (std::size_t u = blockIdx.x; u < units; u += stride) {
+        std::size_t kh, n0;
+        if (!EXACT && a.tc_paths) {
+            const std::uint32_t e = a.tc_rest[u / kSub];
+            kh = e % a.kv_heads;
+            n0 = (e / a.kv_heads) * kTcRows + (u % kSub) * kBlkRows;
+            if (n0 >= a.rows) continue;
+        } else {
+            kh = blockIdx.x % a.kv_heads;
+            n0 = (blockIdx.x / a.kv_heads) * kBlkRows;
+        }
+        const int nrows = static_cast<int>(a.rows - n0 < kBlkRows ? a.rows - n0 : kBlkRows);
+        if (threadIdx.x == 0) {
+            // segments: maximal runs in which row n is the child of row n - 1
+            int nseg = 0;
+            seg_s[0] = 0;
+            std::size_t prev = 0;
+            for (int r = 0; r < nrows; ++r) {
+                const std::size_t n = n0 + r, pos = a.row_pos[n];
+                bad_s[r] = chain_of(a, n, pos) == nullptr;
+                if (r > 0) {
+                    // dense: the parent entry of row n is n - 1; compact: the same
+                    // witness prompt one position further
+                    const bool link = !bad_s[r] && !bad_s[r - 1] && pos == prev + 1 &&
+                                      (a.anc ? a.anc[n * a.anc_stride + pos - 1] == n - 1
+                                             : a.node_prompt[n] == a.node_prompt[n - 1]);
+                    if (!link) seg_s[++nseg] = r;
+                }
+                prev = pos;
+            }
+            seg_s[++nseg] = nrows;
+            nseg_s = nseg;
         }
         __syncthreads();
-        if (done_s) return;
-    }
-    if (threadIdx.x == 0) {
-        // segments: maximal runs in which row n is the child of row n - 1
-        int nseg = 0;
-        seg_s[0] = 0;
-        std::size_t prev = 0;
-        for (int r = 0; r < nrows; ++r) {
-            const std::size_t n = n0 + r, pos = a.row_pos[n];
-            bad_s[r] = chain_of(a, n, pos) == nullptr;
-            if (r > 0) {
-                // dense: the parent entry of row n is n - 1; compact: the same
-                // witness prompt one position further
-                const bool link = !bad_s[r] && !bad_s[r - 1] && pos == prev + 1 &&
-                                  (a.anc ? a.anc[n * a.anc_stride + pos - 1] == n - 1
-                                         : a.node_prompt[n] == a.node_prompt[n - 1]);
-                if (!link) seg_s[++nseg] = r;
+        BlockAttention<EXACT> b{a, smem, reinterpret_cast<std::uint32_t*>(smem + wcap * kCombos),
+                                smem + wcap * kCombos + wcap, tab, red_s, kh,
+                                threadIdx.x, threadIdx.x & 31u, threadIdx.x >> 5};
+        for (int sgi = 0; sgi < nseg_s; ++sgi) {
+            const int r0 = seg_s[sgi], r1 = seg_s[sgi + 1];
+            if (r1 - r0 == 1 && bad_s[r0]) {  // position outside the ancestor table: report, output zeros
+                if (threadIdx.x == 0) flag_check(B2_CHECK_ATTENTION);
+                float* o = a.out + ((n0 + r0) * a.q_heads + kh * kGroup) * 128;
+                for (int i = threadIdx.x; i < kGroup * 128; i += kBlkThreads) o[i] = 0.0f;
+                continue;
             }
-            prev = pos;
+            if (!b.run(n0 + r0, r1 - r0, true))
+                for (int r = r0; r < r1; ++r) b.run(n0 + r, 1, false);
         }
-        seg_s[++nseg] = nrows;
-        nseg_s = nseg;
-    }
-    __syncthreads();
-    BlockAttention<EXACT> b{a, smem, reinterpret_cast<std::uint32_t*>(smem + wcap * kCombos),
-                            smem + wcap * kCombos + wcap, tab, red_s, kh,
-                            threadIdx.x, threadIdx.x & 31u, threadIdx.x >> 5};
-    for (int sgi = 0; sgi < nseg_s; ++sgi) {
-        const int r0 = seg_s[sgi], r1 = seg_s[sgi + 1];
-        if (r1 - r0 == 1 && bad_s[r0]) {  // position outside the ancestor table: report, output zeros
-            if (threadIdx.x == 0) flag_check(B2_CHECK_ATTENTION);
-            float* o = a.out + ((n0 + r0) * a.q_heads + kh * kGroup) * 128;
-            for (int i = threadIdx.x; i < kGroup * 128; i += kBlkThreads) o[i] = 0.0f;
-            continue;
-        }
-        if (!b.run(n0 + r0, r1 - r0, true))
-            for (int r = r0; r < r1; ++r) b.run(n0 + r, 1, false);
+        __syncthreads();  // the shared state is rewritten by the next block
     }
 }
 
@@ -1069,17 +1120,44 @@ int attention_launch(AttnArgs& a, std::size_t head_dim, std::uint32_t flags, b2_
         auto kernel = exact ? attention_tree_block<true> : attention_tree_block<false>;
         if (allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem) != cudaSuccess)
             return launch_result("b2_attention_tree: shared memory attribute");
-        if (!exact && (rows + kTcRows - 1) / kTcRows * kv_heads <= 0x7FFFFFFFu) {
-            // tree order: the path blocks on the tensor cores first; the block
-            // kernel below then takes only the rows of the other blocks
-            if (allow_dynamic_smem(reinterpret_cast<const void*>(attention_tree_tc), kTcSmem) != cudaSuccess)
-                return launch_result("b2_attention_tree: shared memory attribute");
-            launch_pdl(attention_tree_tc, static_cast<unsigned>((rows + kTcRows - 1) / kTcRows * kv_heads), kTcThreads,
-                       kTcSmem, s, a);
-            a.tc_paths = 1;
+        // tree order: the path blocks on the tensor cores first, from the hi /
+        // lo planes of K and V in stream-ordered scratch (then the count and
+        // list of the blocks left over); the block kernel below then strides
+        // over the rows of the blocks left over
+        void* scratch = nullptr;
+        const std::size_t n4 = rows * kv_heads * 32;  // float4s per plane
+        const std::size_t tc_blocks = (rows + kTcRows - 1) / kTcRows * kv_heads;
+        const std::size_t scratch_bytes = 4 * n4 * sizeof(float4) + (1 + tc_blocks) * sizeof(std::uint32_t);
+        unsigned grid = static_cast<unsigned>((rows + kBlkRows - 1) / kBlkRows * kv_heads);
+        if (!exact && tc_blocks <= 0x7FFFFFFFu) {
+            if (scratch_alloc(&scratch, scratch_bytes, s) != cudaSuccess) {
+                cudaGetLastError();  // no scratch: every block on the block kernel
+                scratch = nullptr;
+            }
         }
-        launch_pdl(kernel, static_cast<unsigned>((rows + kBlkRows - 1) / kBlkRows * kv_heads), kBlkThreads, smem,
-                   s, a, wcap);
+        if (scratch) {
+            if (allow_dynamic_smem(reinterpret_cast<const void*>(attention_tree_tc), kTcSmem) != cudaSuccess) {
+                cudaFreeAsync(scratch, s);
+                return launch_result("b2_attention_tree: shared memory attribute");
+            }
+            float4* split = static_cast<float4*>(scratch);
+            std::uint32_t* rest_count = reinterpret_cast<std::uint32_t*>(split + 4 * n4);
+            std::uint32_t* rest = rest_count + 1;
+            const std::size_t want = (n4 + 255) / 256;
+            launch_pdl(tc_split_kv, static_cast<unsigned>(want < 148 * 8 ? want : 148 * 8), 256, 0, s,
+                       reinterpret_cast<const float4*>(k), reinterpret_cast<const float4*>(v), split, n4, rest_count);
+            launch_pdl(attention_tree_tc, static_cast<unsigned>(tc_blocks), kTcThreads, kTcSmem, s, a,
+                       static_cast<const float*>(scratch), rest_count, rest);
+            a.tc_paths = 1;
+            a.tc_rest_count = rest_count;
+            a.tc_rest = rest;
+            const std::size_t wave = static_cast<std::size_t>(sm_count()) *
+                                     static_cast<std::size_t>(resident_ctas(reinterpret_cast<const void*>(kernel),
+                                                                            kBlkThreads, smem));
+            grid = static_cast<unsigned>(wave < grid ? wave : grid);
+        }
+        launch_pdl(kernel, grid, kBlkThreads, smem, s, a, wcap);
+        if (scratch) cudaFreeAsync(scratch, s);
         return launch_result("b2_attention_tree");
     }
     int rc;

@@ -40,6 +40,13 @@ __host__ __device__ inline bool aligned16(const void* p) {
 // Number of SMs of the current device (148 on B200), cached per device.
 int sm_count();
 
+// Stream-ordered device scratch of `bytes`: from a memory pool of this
+// library on the current device that keeps its memory reserved between
+// calls (so a repeated call does not go back to the driver), or, while
+// `stream` is being captured, a graph allocation (cudaMallocAsync). Free it
+// with cudaFreeAsync on the same stream.
+cudaError_t scratch_alloc(void** p, std::size_t bytes, cudaStream_t stream);
+
 // Gated SiLU launch (moe.cu) with the exponential mode chosen by the caller:
 // b2_silu_mul passes exact = true (bit-exact always); b2_silu_mul_flags and
 // b2_prefill_layers the mode of their flags.
