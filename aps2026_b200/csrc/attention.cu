@@ -258,54 +258,61 @@ attention_tree_kernel(AttnArgs a) {
 // 1e-6 absolute of the reference, so its contractions run on the tcgen05
 // tensor cores with FP32-level products: every operand x is split into
 // hi = x rounded to TF32 and lo = (x - hi) rounded to TF32, and each product
-// is lo.hi + hi.lo + hi.hi -- three kind::tf32 MMAs into one FP32
-// accumulator in tensor memory (relative error ~2^-22 per product).
+// is hi.hi + hi.lo + lo.hi -- kind::tf32 MMAs with FP32 accumulators in
+// tensor memory (relative error ~2^-22 per product).
 //
 // tc_split_kv writes the hi / lo planes of K and V once per call. One CTA of
 // attention_tree_tc per (block of 32 consecutive trie rows that form a path,
 // KV head): M = 32 rows x 4 query heads = 128 rows of the MMA, and the keys
 // of every row are a prefix of the deepest row's chain, so each 32-key tile
 // of that chain is staged once for all 128 rows.
-//   tensor memory  Q hi / lo [128 x 128] (the A operand of S = Q K^T), S
-//                  [128 x 32] twice, P hi / lo [128 x 32] (the A operand of
-//                  P V), the tile's P V [128 x 128];
-//   shared memory  a ring of 3 key tiles hi / lo [32 keys x 128 dims]
-//                  (K-major, 128-byte swizzle) and a ring of 2 value tiles
-//                  hi / lo [32 keys x 128 dims] (the B operand of P V with
-//                  its N = dims contiguous: MN-major, 128-byte rows with
-//                  32-byte swizzle granules); O [128 dims / 4][128 MMA rows]
-//                  float4s.
-// Warp roles: 4 stages key tiles, 5 value tiles (16-byte cp.async copies
-// of the planes into the swizzled layouts); 6 issues the MMAs -- S(t + 2)
-// as soon as S(t) has been read, P V(t) once P(t) is written; 0-3 own one
-// MMA row each (thread m: row m / 4 of the block, query head m % 4 of the
-// group, tensor-memory lane m) and run the softmax online in base 2: with
-// s2 = s * scale * log2(e) per key, the row's running maximum m and sum l
-// are updated per tile (l = l * 2^(m_old - m) + sum p, p = 2^(s2 - m), 0
-// outside the row's window), and the previous tile's P V is folded into O
-// as O = O * 2^(m_old - m) + PV in FP32 round-to-nearest (the tensor core's
-// accumulator truncates; chaining every tile there biased long windows by
-// ~1e-6). The epilogue writes O * (1 / l): the softmax of the tree-order
-// SIMT kernel, formed in another order. Blocks that are not a path (prompt
-// boundaries, shared-prefix branch points) are left to attention_tree_block,
-// which skips the path blocks by the same test.
+//   tensor memory  Q hi / lo [128 x 128] (the A operands of the scores), S
+//                  [128 x 64]: columns 0-31 Qh.Kh, 32-63 Qh.Kl + Ql.Kh (one
+//                  N = 64 MMA per k-step against the stacked [Kh; Kl] tile
+//                  costs what an N = 32 one does), P hi / lo [128 x 32] (the
+//                  A operand of P V), the tile's P V [128 x 128];
+//   shared memory  a ring of 2 key tiles, per 32-dim block the hi then the
+//                  lo rows of the 32 keys (K-major, 128-byte swizzle), and a
+//                  ring of 2 value tiles hi / lo [32 keys x 128 dims] (the B
+//                  operand of P V with N = dims contiguous: MN-major,
+//                  128-byte rows with 32-byte swizzle granules); O [128 dims
+//                  / 4][128 MMA rows] float4s.
+// Warp roles: 8-9 stage key tiles, 10-11 value tiles (16-byte cp.async
+// copies of the planes into the swizzled layouts); 12 issues the MMAs --
+// S(t + 1) as soon as S(t) has been read, P V(t) once P(t) is written; 0-7
+// run the softmax, two threads per MMA row m (tensor-memory lane m: row m / 4
+// of the block, query head m % 4 of the group), thread half h taking keys
+// 16h .. 16h + 15 of each tile and dims 64h .. 64h + 63 of O. The softmax is
+// online in base 2: with s2 = s * scale * log2(e) per key, the row's
+// running maximum m (the pair exchanges its halves' maxima once per tile)
+// and sum l are updated per tile (l = l * 2^(m_old - m) + sum p,
+// p = 2^(s2 - m), 0 outside the row's window), and the previous tile's P V
+// is folded into O as O = O * 2^(m_old - m) + PV in FP32 round-to-nearest
+// (the tensor core's accumulator truncates; chaining every tile there biased
+// long windows by ~1e-6). The epilogue writes O * (1 / l): the softmax of
+// the tree-order SIMT kernel, formed in another order. Blocks that are not a
+// path (prompt boundaries, shared-prefix branch points) are listed for
+// attention_tree_block.
 constexpr int kTcRows = 32;  // trie rows per CTA (x 4 heads = M 128)
 constexpr int kTcKeys = 32;  // chain keys per tile
-constexpr int kTcSoftmaxThreads = 128;                      // warps 0-3
-constexpr int kTcThreads = kTcSoftmaxThreads + 3 * 32;      // + key, value and MMA warps
-constexpr int kTcKStages = 3, kTcVStages = 2;
+constexpr int kTcSoftmaxThreads = 256;  // warps 0-7
+constexpr int kTcStageWarps = 2;        // per operand
+constexpr int kTcStageThreads = 32 * kTcStageWarps;
+constexpr int kTcThreads = kTcSoftmaxThreads + 2 * kTcStageThreads + 32;  // + key, value and MMA warps
+constexpr int kTcKStages = 2, kTcVStages = 2;
 constexpr std::uint32_t kColQh = 0, kColQl = 128, kColO = 256, kColS = 384, kColPh = 448, kColPl = 480;
 constexpr std::uint32_t kTcCols = 512;
-constexpr int kTcTileBytes = 16 * 1024;  // one operand tile: 32 x 128 fp32
+constexpr int kTcTileBytes = 16 * 1024;  // one operand plane of a tile: 32 x 128 fp32
 constexpr int kTcStageBytes = 2 * kTcTileBytes;  // hi, lo
-// rings + O + 1024-byte alignment (225 KB: one CTA per SM, each allocating
+// rings + O + 1024-byte alignment (193 KB: one CTA per SM, each allocating
 // all 512 tensor-memory columns)
 constexpr std::size_t kTcSmem = (kTcKStages + kTcVStages) * kTcStageBytes + 128 * 128 * 4 + 1024;
 
-// Byte offset of dims 4c .. 4c + 3 of key j in a key tile: K-major rows of
-// 128 bytes (32 dims), 8-key atoms of 1024 bytes, the four 32-dim blocks
-// 4096 bytes apart, 16-byte chunks swizzled by j % 8.
-__device__ __forceinline__ int tc_key_offset(int j, int c) { return (c >> 3) * 4096 + tc::sw128_offset(j, c & 7); }
+// Byte offset of dims 4c .. 4c + 3 of key j's hi row in a key stage: per
+// 32-dim block (8192 bytes) the 32 hi rows then the 32 lo rows (the lo row
+// is 4096 bytes further), K-major rows of 128 bytes in 8-row atoms of 1024
+// bytes, 16-byte chunks swizzled by j % 8.
+__device__ __forceinline__ int tc_key_offset(int j, int c) { return (c >> 3) * 8192 + tc::sw128_offset(j, c & 7); }
 // ... in a value tile: rows of 128 bytes (32 dims) per key, 4-key groups of
 // 512 bytes, the four 32-dim blocks 4096 bytes apart, 32-byte granules
 // swizzled by j % 4 (the MN-major SWIZZLE_128B_BASE32B layout).
@@ -443,7 +450,9 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
     extern __shared__ __align__(16) unsigned char tc_raw[];
     __shared__ std::uint32_t tmem_base;
     __shared__ __align__(8) std::uint64_t kfull[kTcKStages], kempty[kTcKStages], vfull[kTcVStages],
-        vempty[kTcVStages], sfull[2], sempty[2], qfull, pfull, ofull;
+        vempty[kTcVStages], sfull, sempty, qfull, pfull, ofull;
+    __shared__ float max_x[2][2][128];  // [tile % 2][half][MMA row]: the halves' tile maxima
+    __shared__ float sum_x[2][128];     // [half][MMA row]: the halves' sums
     __shared__ int path_s;
     __shared__ volatile int abort_s;
     __shared__ std::size_t pos0_s;
@@ -467,17 +476,15 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
             pos0_s = p0;
             abort_s = 0;
             for (int s = 0; s < kTcKStages; ++s) {
-                mbar_init(&kfull[s], 32);
+                mbar_init(&kfull[s], kTcStageThreads);
                 mbar_init(&kempty[s], 1);
             }
             for (int s = 0; s < kTcVStages; ++s) {
-                mbar_init(&vfull[s], 32);
+                mbar_init(&vfull[s], kTcStageThreads);
                 mbar_init(&vempty[s], 1);
             }
-            for (int s = 0; s < 2; ++s) {
-                mbar_init(&sfull[s], 1);
-                mbar_init(&sempty[s], kTcSoftmaxThreads);
-            }
+            mbar_init(&sfull, 1);
+            mbar_init(&sempty, kTcSoftmaxThreads);
             mbar_init(&qfull, kTcSoftmaxThreads);
             mbar_init(&pfull, kTcSoftmaxThreads);
             mbar_init(&ofull, 1);
@@ -500,14 +507,16 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
     const int tiles_n = static_cast<int>((last - kb0 + kTcKeys) / kTcKeys);
     const std::size_t kv_row = a.kv_heads * 128;
     constexpr unsigned kSoftmaxWarps = kTcSoftmaxThreads / 32;
+    constexpr unsigned kMmaWarp = kSoftmaxWarps + 2 * kTcStageWarps;
 
-    if (warp == kSoftmaxWarps || warp == kSoftmaxWarps + 1) {
-        // ---- staging: warp 4 the key tiles into a ring of 3, warp 5 the value
-        // tiles into a ring of 2; lane = 16-byte chunk c of a key's 128 dims.
-        // Each lane's copies of a tile arrive on the stage's barrier when they
-        // have landed (cp.async.mbarrier.arrive.noinc: one of its 32
-        // arrivals). ----
-        const bool keys = warp == kSoftmaxWarps;
+    if (warp >= kSoftmaxWarps && warp < kMmaWarp) {
+        // ---- staging: warps 8-9 the key tiles into a ring of 2, 10-11 the
+        // value tiles into a ring of 2; warp w takes keys 16 (w % 2) .. + 15,
+        // lane = 16-byte chunk c of a key's 128 dims. Each lane's copies of a
+        // tile arrive on the stage's barrier when they have landed
+        // (cp.async.mbarrier.arrive.noinc: one of its 64 arrivals). ----
+        const bool keys = warp < kSoftmaxWarps + kTcStageWarps;
+        const int j0 = static_cast<int>((warp - kSoftmaxWarps) % kTcStageWarps) * (kTcKeys / kTcStageWarps);
         const int stages = keys ? kTcKStages : kTcVStages;
         unsigned char* ring = keys ? kring : vring;
         std::uint64_t* full = keys ? kfull : vfull;
@@ -515,53 +524,52 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
         const std::size_t plane = a.rows * kv_row;
         const float* hi_p = split + (keys ? 0 : 2 * plane) + kh * 128 + 4 * lane;
         const float* lo_p = hi_p + plane;
+        const int lo_off = keys ? 4096 : kTcTileBytes;  // the lo row of a chunk, from its hi row
         for (int t = 0; t < tiles_n; ++t) {
             const int s = t % stages;
             if (t >= stages && !__all_sync(0xffffffffu, tc_wait(&empty[s], ((t / stages) - 1) & 1, &abort_s)))
                 break;
-            unsigned char* hi_t = ring + s * kTcStageBytes;
-            unsigned char* lo_t = hi_t + kTcTileBytes;
+            unsigned char* st = ring + s * kTcStageBytes;
             const std::uint32_t r = tc_key_row(a, chain, kb0 + static_cast<std::size_t>(t) * kTcKeys + lane, last, n0);
 #pragma unroll 8
-            for (int j = 0; j < kTcKeys; ++j) {
+            for (int i = 0; i < kTcKeys / kTcStageWarps; ++i) {
+                const int j = j0 + i;
                 const std::uint32_t rk = __shfl_sync(0xffffffffu, r, j);
                 const bool valid = rk != 0xFFFFFFFFu;
                 const std::size_t src = valid ? rk * kv_row : 0;
                 const int off = keys ? tc_key_offset(j, static_cast<int>(lane)) : tc_value_offset(j, static_cast<int>(lane));
-                tc_copy16(hi_t + off, hi_p + src, valid);
-                tc_copy16(lo_t + off, lo_p + src, valid);
+                tc_copy16(st + off, hi_p + src, valid);
+                tc_copy16(st + off + lo_off, lo_p + src, valid);
             }
             asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(&full[s])) : "memory");
         }
         asm volatile("cp.async.wait_all;" ::: "memory");  // none in flight when the CTA ends
-    } else if (warp == kSoftmaxWarps + 2) {
+    } else if (warp == kMmaWarp) {
         // ---- MMA issue (one thread) ----
         if (lane == 0) {
-            // S(t) = Ql Kh + Qh Kl + Qh Kh into S buffer t % 2
+            // S(t): Qh . [Kh; Kl] (N = 64) into columns 0-63, then Ql . Kh
+            // (N = 32) added to columns 32-63
             auto scores = [&](int t) -> bool {
                 const int s = t % kTcKStages;
-                if (t >= 2 && !tc_wait(&sempty[t & 1], ((t >> 1) - 1) & 1, &abort_s)) return false;
                 if (!tc_wait(&kfull[s], (t / kTcKStages) & 1, &abort_s)) return false;
                 tc::fence_after_sync();
-                constexpr std::uint32_t idesc = tc::tf32_idesc(128, kTcKeys);
-                const unsigned char* k_hi = kring + s * kTcStageBytes;
-                const unsigned char* kb[3] = {k_hi, k_hi + kTcTileBytes, k_hi};
-                const std::uint32_t qa[3] = {kColQl, kColQh, kColQh};
-                const std::uint32_t d = tmem + kColS + 32u * static_cast<std::uint32_t>(t & 1);
-                for (int part = 0; part < 3; ++part)
-                    for (int ks = 0; ks < 16; ++ks)
-                        tc::mma_tf32_ts(d, tmem + qa[part] + ks * 8,
-                                        tc::sw128_desc(kb[part] + (ks >> 2) * 4096 + (ks & 3) * 32), idesc,
-                                        part > 0 || ks > 0);
-                tc::commit(&sfull[t & 1]);
+                const unsigned char* kst = kring + s * kTcStageBytes;
+                for (int ks = 0; ks < 16; ++ks)
+                    tc::mma_tf32_ts(tmem + kColS, tmem + kColQh + ks * 8,
+                                    tc::sw128_desc(kst + (ks >> 2) * 8192 + (ks & 3) * 32), tc::tf32_idesc(128, 64),
+                                    ks > 0);
+                for (int ks = 0; ks < 16; ++ks)
+                    tc::mma_tf32_ts(tmem + kColS + 32, tmem + kColQl + ks * 8,
+                                    tc::sw128_desc(kst + (ks >> 2) * 8192 + (ks & 3) * 32), tc::tf32_idesc(128, 32),
+                                    true);
+                tc::commit(&sfull);
                 if (t + kTcKStages < tiles_n) tc::commit(&kempty[s]);
                 return true;
             };
-            bool ok = tc_wait(&qfull, 0, &abort_s);
-            ok = ok && scores(0);
-            if (ok && tiles_n > 1) ok = scores(1);
+            bool ok = tc_wait(&qfull, 0, &abort_s) && scores(0);
             for (int t = 0; t < tiles_n && ok; ++t) {
-                if (t + 2 < tiles_n && !scores(t + 2)) break;  // waits until S(t) has been read
+                // S(t + 1) once every softmax thread has read S(t)
+                if (t + 1 < tiles_n && !(tc_wait(&sempty, t & 1, &abort_s) && scores(t + 1))) break;
                 // P V(t) = Pl Vh + Ph Vl + Ph Vh (B = V MN-major), once P(t) is in tensor memory
                 const int s = t % kTcVStages;
                 if (!tc_wait(&pfull, t & 1, &abort_s) || !tc_wait(&vfull[s], (t / kTcVStages) & 1, &abort_s)) break;
@@ -580,15 +588,16 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
         }
         __syncwarp();
     } else {
-        // ---- softmax warps ----
-        const std::uint32_t lane_base = static_cast<std::uint32_t>(warp * 32) << 16;
-        const int ri = static_cast<int>(tid >> 2), hg = static_cast<int>(tid & 3);  // this thread's row and head
+        // ---- softmax warps: thread (m, h), m = MMA row / tensor-memory lane ----
+        const unsigned m = tid & 127u, h = tid >> 7;
+        const std::uint32_t lane_base = static_cast<std::uint32_t>((warp & 3u) * 32) << 16;
+        const int ri = static_cast<int>(m >> 2), hg = static_cast<int>(m & 3);  // this row and head
         const bool row_ok = ri < nr;
         const std::size_t pos_i = pos0 + ri;
-        // Q hi / lo into tensor memory (lane tid, 128 columns each); O = 0
+        // Q hi / lo, dims 64h .. 64h + 63, into tensor memory; this half of O = 0
         {
-            const float* qr = a.q + ((n0 + (row_ok ? ri : 0)) * a.q_heads + kh * kGroup + hg) * 128;
-            for (int c0 = 0; c0 < 128; c0 += 32) {
+            const float* qr = a.q + ((n0 + (row_ok ? ri : 0)) * a.q_heads + kh * kGroup + hg) * 128 + 64 * h;
+            for (int c0 = 0; c0 < 64; c0 += 32) {
                 float hi[32], lo[32];
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
@@ -598,22 +607,22 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
                     tc_split(v.z, hi[j + 2], lo[j + 2]);
                     tc_split(v.w, hi[j + 3], lo[j + 3]);
                 }
-                tc::st32(tmem + lane_base + kColQh + c0, hi);
-                tc::st32(tmem + lane_base + kColQl + c0, lo);
+                tc::st32(tmem + lane_base + kColQh + 64 * h + c0, hi);
+                tc::st32(tmem + lane_base + kColQl + 64 * h + c0, lo);
             }
             tc::st_wait();
             tc::fence_before_sync();
             mbar_arrive(&qfull);
-            for (int c = 0; c < 32; ++c) oacc[c * kTcSoftmaxThreads + tid] = zero4();
+            for (int c = 0; c < 16; ++c) oacc[(16 * h + c) * 128 + m] = zero4();
         }
-        // folds the P V of the tile issued last into O: O = O * alpha + PV
+        // folds this half of the P V of the tile issued last into O: O = O * alpha + PV
         auto fold = [&](float alpha) {
-            for (int c0 = 0; c0 < 128; c0 += 32) {
+            for (int c0 = 0; c0 < 64; c0 += 32) {
                 float o[32];
-                tc::ld32(tmem + lane_base + kColO + c0, o);
+                tc::ld32(tmem + lane_base + kColO + 64 * h + c0, o);
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    float4* dst = oacc + ((c0 >> 2) + q) * kTcSoftmaxThreads + tid;
+                    float4* dst = oacc + (16 * h + (c0 >> 2) + q) * 128 + m;
                     float4 x = *dst;
                     x.x = __fmaf_rn(x.x, alpha, o[4 * q]);
                     x.y = __fmaf_rn(x.y, alpha, o[4 * q + 1]);
@@ -624,56 +633,69 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
             }
         };
         const float scale2 = __fmul_rn(a.scale, 1.4426950408889634f);  // scale * log2(e)
-        // the keys kb0 + lo_k .. kb0 + hi_k are in this row's window
+        // keys kb0 + lo_k .. kb0 + hi_k are in this row's window
         const long long lo_k = row_ok ? static_cast<long long>(pos_i + 1 > a.window ? pos_i + 1 - a.window : 0) -
                                             static_cast<long long>(kb0)
                                       : 1;
         const long long hi_k = row_ok ? static_cast<long long>(pos_i - kb0) : 0;
-        float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
+        float mx = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
         bool ok = true;
-        for (int t = 0; t < tiles_n && ok; ++t) {
-            ok = __all_sync(0xffffffffu, tc_wait(&sfull[t & 1], (t >> 1) & 1, &abort_s));
-            if (!ok) break;
-            tc::fence_after_sync();
-            float ph[32], pl[32];
-            tc::ld32(tmem + lane_base + kColS + 32u * static_cast<std::uint32_t>(t & 1), ph);
-            tc::fence_before_sync();
-            mbar_arrive(&sempty[t & 1]);  // S(t + 2) may be computed into this buffer
-            // window of this row within the tile: j in [jlo, jhi]
-            const long long t0 = static_cast<long long>(t) * kTcKeys;
-            const int jlo = static_cast<int>(lo_k - t0 < 0 ? 0 : (lo_k - t0 > 32 ? 32 : lo_k - t0));
-            const int jhi = static_cast<int>(hi_k - t0 > 31 ? 31 : (hi_k - t0 < -1 ? -1 : hi_k - t0));
+        for (int t = 0; t < tiles_n; ++t) {
+            float p[16], pl[16];
             float mt = -INFINITY;
+            if (ok) ok = __all_sync(0xffffffffu, tc_wait(&sfull, t & 1, &abort_s));
+            if (ok) {
+                tc::fence_after_sync();
+                float x[16];
+                tc::ld16(tmem + lane_base + kColS + 16 * h, p);        // Qh.Kh
+                tc::ld16(tmem + lane_base + kColS + 32 + 16 * h, x);   // Qh.Kl + Ql.Kh
+                tc::fence_before_sync();
+                mbar_arrive(&sempty);  // S(t + 1) may be computed into these columns
+                // this row's window within the tile: keys jlo .. jhi of it
+                const long long t0 = static_cast<long long>(t) * kTcKeys + 16 * h;
+                const int jlo = static_cast<int>(lo_k - t0 < 0 ? 0 : (lo_k - t0 > 16 ? 16 : lo_k - t0));
+                const int jhi = static_cast<int>(hi_k - t0 > 15 ? 15 : (hi_k - t0 < -1 ? -1 : hi_k - t0));
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                ph[j] = (j >= jlo && j <= jhi) ? __fmul_rn(ph[j], scale2) : -INFINITY;
-                mt = fmaxf(mt, ph[j]);
+                for (int j = 0; j < 16; ++j) {
+                    p[j] = (j >= jlo && j <= jhi) ? __fmul_rn(__fadd_rn(p[j], x[j]), scale2) : -INFINITY;
+                    mt = fmaxf(mt, p[j]);
+                }
+                max_x[t & 1][h][m] = mt;
             }
-            const float mn = fmaxf(m, mt);
+            // the pair's maxima meet here; also the group-wide decision to stop
+            if (softmax_group_any(!ok)) {
+                ok = false;
+                break;
+            }
+            mt = fmaxf(mt, max_x[t & 1][h ^ 1u][m]);
+            const float mn = fmaxf(mx, mt);
             const float mref = mn == -INFINITY ? 0.0f : mn;
-            const float alpha = tc_exp2(__fsub_rn(m, mref));  // 0 while m is -inf, 1 while it holds
+            const float alpha = tc_exp2(__fsub_rn(mx, mref));  // 0 while mx is -inf, 1 while it holds
             float l0 = 0.0f, l1 = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-                const float p0 = tc_exp2(__fsub_rn(ph[j], mref));
-                const float p1 = tc_exp2(__fsub_rn(ph[j + 1], mref));
+            for (int j = 0; j < 16; j += 2) {
+                const float p0 = tc_exp2(__fsub_rn(p[j], mref));
+                const float p1 = tc_exp2(__fsub_rn(p[j + 1], mref));
                 l0 = __fadd_rn(l0, p0);
                 l1 = __fadd_rn(l1, p1);
-                tc_split(p0, ph[j], pl[j]);
-                tc_split(p1, ph[j + 1], pl[j + 1]);
+                tc_split(p0, p[j], pl[j]);
+                tc_split(p1, p[j + 1], pl[j + 1]);
             }
             l = __fmaf_rn(l, alpha, __fadd_rn(l0, l1));
-            m = mn;
+            mx = mn;
             if (t > 0) {  // P V(t - 1) done: fold it, and P's columns are free
                 ok = __all_sync(0xffffffffu, tc_wait(&ofull, (t - 1) & 1, &abort_s));
-                if (!ok) break;
-                tc::fence_after_sync();
-                fold(alpha_prev);
+                if (ok) {
+                    tc::fence_after_sync();
+                    fold(alpha_prev);
+                }
             }
             alpha_prev = alpha;
-            tc::st32(tmem + lane_base + kColPh, ph);
-            tc::st32(tmem + lane_base + kColPl, pl);
-            tc::st_wait();
+            if (ok) {
+                tc::st16(tmem + lane_base + kColPh + 16 * h, p);
+                tc::st16(tmem + lane_base + kColPl + 16 * h, pl);
+                tc::st_wait();
+            }
             tc::fence_before_sync();
             mbar_arrive(&pfull);  // also: this thread's reads of the P V columns are done
         }
@@ -684,12 +706,14 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
                 fold(alpha_prev);
             }
         }
-        // ---- epilogue: out = O / l ----
+        // ---- epilogue: out = O / l, l the sum of the halves' sums ----
+        sum_x[h][m] = l;
         if (!softmax_group_any(!ok) && row_ok) {
-            const float inv = __fdiv_rn(1.0f, l);
-            float4* orow = reinterpret_cast<float4*>(a.out + ((n0 + ri) * a.q_heads + kh * kGroup + hg) * 128);
-            for (int c = 0; c < 32; ++c) {
-                const float4 x = oacc[c * kTcSoftmaxThreads + tid];
+            const float inv = __fdiv_rn(1.0f, __fadd_rn(sum_x[0][m], sum_x[1][m]));
+            float4* orow =
+                reinterpret_cast<float4*>(a.out + ((n0 + ri) * a.q_heads + kh * kGroup + hg) * 128 + 64 * h);
+            for (int c = 0; c < 16; ++c) {
+                const float4 x = oacc[(16 * h + c) * 128 + m];
                 st_plain(orow + c, make_float4(__fmul_rn(x.x, inv), __fmul_rn(x.y, inv), __fmul_rn(x.z, inv),
                                                __fmul_rn(x.w, inv)));
             }
