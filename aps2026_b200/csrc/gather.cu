@@ -132,7 +132,12 @@ gather_rows_bulk(const float* __restrict__ x, std::size_t x_rows, std::size_t h,
             if (lane == 0) {
                 flag_check(B2_CHECK_WAIT);
                 // the loads issued so far (units up to k + kBulkStages - 2, or the
-                // first kBulkStages when k == 0) may still land
+                // first kBulkStages when k == 0) may still land: one bounded wait
+                // each on their barriers, the only completion signal a global ->
+                // shared bulk copy has, then the stores' bulk group. A wait that
+                // gives up again means the copy engine has stopped; an unbounded
+                // wait would hang the GPU, so the warp returns and B2_CHECK_WAIT
+                // tells the host that the context is no longer usable.
                 const std::size_t issued = k == 0 ? kBulkStages : k + kBulkStages - 1;
                 for (std::size_t j = k; j < n && j < issued; ++j)
                     mbar_wait(&bar[j % kBulkStages], static_cast<unsigned>((j / kBulkStages) & 1u));

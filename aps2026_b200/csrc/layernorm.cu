@@ -303,7 +303,14 @@ ln_rows_bulk(LnArgs a) {
         if (__syncthreads_or(!mbar_wait(&bar, parity))) {  // a copy never landed: stop, report
             if (threadIdx.x == 0) {
                 flag_check(B2_CHECK_WAIT);
-                mbar_wait(&bar, parity);  // one more bounded wait for the copies in flight
+                // One more bounded wait for the copies in flight. A global ->
+                // shared bulk copy that completes on an mbarrier has no other
+                // completion signal (cp.async.bulk.wait_group tracks bulk-group
+                // copies only), and an unbounded wait would hang the GPU; if this
+                // wait also gives up, the copy engine has stopped, the CTA
+                // returns, and B2_CHECK_WAIT tells the host that the context is
+                // no longer usable (b2_device_status).
+                mbar_wait(&bar, parity);
             }
             return;
         }
