@@ -215,6 +215,14 @@ int b2_causal_softmax(const float* scores, float* probs, size_t heads,
  * B2_FLAG_EXACT_ORDER, within tolerance with tree-order softmax sums.
  * A row whose position is >= anc_stride, or a chain entry >= rows, is
  * reported through b2_device_status (B2_CHECK_ATTENTION).
+ * Without B2_FLAG_EXACT_ORDER and at head_dim 128, blocks of 32 trie rows
+ * that form a path run on the tensor cores (three TF32 products per FP32
+ * product) from TF32 hi / lo copies of k and v in stream-ordered scratch of
+ * 16 * rows * kv_heads * 128 + 4 * (rows / 32 + 2) * kv_heads bytes, taken
+ * from a memory pool the library keeps per device (its memory stays
+ * reserved between calls) or, during stream capture, a graph allocation;
+ * the scratch is freed on `stream` after the launches. If it cannot be had,
+ * every block runs on the CUDA cores instead.
  */
 int b2_attention_tree(const float* q, const float* k, const float* v,
                       float* out, const uint32_t* row_pos,
