@@ -24,12 +24,14 @@ def _case(seed, prompts, length, shared, q_heads=16, kv_heads=4, hd=128):
     return t, q, k, v
 
 
-# head_dim 128 runs the query-blocked kernel (4 path rows per CTA), 64 the
-# per-row kernel; lengths not divisible by 4 leave partial blocks and blocks
-# that straddle prompt starts; window 100 < depth.
+# head_dim 128 runs the query-blocked kernel (4 path rows per CTA) and, in tree
+# order, the tensor-core kernel on 32-row path blocks; 64 the per-row kernel;
+# lengths not divisible by 4 or 32 leave partial blocks and blocks that
+# straddle prompt starts (30 prompts of 9 tokens: nearly every 32-row block is
+# left to the CUDA-core kernel); window 100 < depth.
 @pytest.mark.parametrize("prompts,length,shared,window,hd", [(3, 300, 40, 2047, 128), (2, 700, 10, 100, 128),
                                                               (1, 5, 0, 2047, 128), (5, 37, 3, 2047, 128),
-                                                              (3, 130, 20, 50, 64)])
+                                                              (30, 9, 2, 2047, 128), (3, 130, 20, 50, 64)])
 @pytest.mark.parametrize("exact", [True, False])
 def test_attention_tree_vs_oracle(cuda, prompts, length, shared, window, hd, exact):
     import torch
@@ -189,3 +191,87 @@ def test_packed_segments_match_reference_grouped_kernel(cuda):
                                    exact=True)
     torch.cuda.synchronize()
     oracle.assert_bitexact(to_host(out), to_host(ref), "compact chains vs k_attention_grouped_gqa4")
+
+
+def _compact_case(cuda, seed, prompts_n, max_len, shared):
+    import torch
+
+    from aps2026_b200 import ops
+
+    g = rng(seed)
+    base = g.integers(0, 500, shared)
+    prompts = [np.concatenate([base[:int(g.integers(0, shared + 1))], g.integers(0, 500, int(g.integers(1, max_len)))])
+               .astype(np.int32) for _ in range(prompts_n)]
+    offs = np.zeros(len(prompts) + 1, np.int32)
+    offs[1:] = np.cumsum([len(p) for p in prompts])
+    offs_d = torch.from_numpy(offs).to(cuda)
+    dt = ops.prefix_trie_device(torch.from_numpy(np.concatenate(prompts)).to(cuda), offs_d, vocab=500)
+    R = dt.nodes
+    q, k, v = (to_dev(normal(g, (R, n * 128)), cuda) for n in (16, 4, 4))
+    stride = max(len(p) for p in prompts)
+    return dict(q=q, k=k, v=v, pos=dt.node_depth, prompt=dt.node_prompt, offs=offs_d, token_node=dt.token_node,
+                stride=stride, rows=R)
+
+
+def _run_compact(c, exact, out=None):
+    import torch
+
+    from aps2026_b200 import ops
+
+    out = torch.full_like(c["q"], float("nan")) if out is None else out
+    ops.attention_tree_compact_gpu(c["q"], c["k"], c["v"], out, c["pos"], c["prompt"], c["offs"], c["token_node"],
+                                   c["stride"], c["rows"], 16, 4, 128, 2047, exact=exact)
+    return out
+
+
+def test_attention_tree_order_compact_scratch_reuse(cuda):
+    """Tree order with compact chains, three calls in a row -- a large batch,
+    a small one, the large one again -- so the tensor-core path's scratch
+    comes from the library's pool at two sizes: every output within the
+    tolerance of the exact-order output, and the repeated call bit-identical
+    to the first."""
+    import torch
+
+    from aps2026_b200 import ops
+
+    big = _compact_case(cuda, 56, 12, 900, 300)
+    small = _compact_case(cuda, 57, 5, 120, 40)
+    first = _run_compact(big, False)
+    mid = _run_compact(small, False)
+    again = _run_compact(big, False)
+    want_big, want_small = _run_compact(big, True), _run_compact(small, True)
+    torch.cuda.synchronize()
+    oracle.assert_close(to_host(first), to_host(want_big), what="tree order vs exact order (large batch)")
+    oracle.assert_close(to_host(mid), to_host(want_small), what="tree order vs exact order (small batch)")
+    assert torch.equal(first, again)
+    assert ops.device_status() == 0
+
+
+def test_attention_tree_order_under_graph_capture(cuda):
+    """The tree-order call captured in a CUDA graph (its scratch becomes a
+    graph allocation) and replayed twice gives the eager call's outputs, bit
+    for bit."""
+    import torch
+
+    from aps2026_b200 import ops
+
+    c = _compact_case(cuda, 58, 8, 500, 200)
+    eager = _run_compact(c, False)
+    torch.cuda.synchronize()
+    out = torch.full_like(c["q"], float("nan"))
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        _run_compact(c, False, out)  # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        _run_compact(c, False, out)
+    for _ in range(2):
+        out.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    del graph
+    assert ops.device_status() == 0
