@@ -363,7 +363,7 @@ ln_rows_bulk(LnArgs a) {
 // batches of 16 rows and "ticks" of one 128-float chunk of each row:
 //
 //   compute warps   stage, a ring of shared-memory stages ahead (8 stages
-//                   for plain LN, 5 with the residual, 4 with the
+//                   for plain LN, 6 with the residual, 5 with the
 //                   un-permute, as many as fit), the pass-A inputs of batch
 //                   b (x; x and the residual; or the carry and the two
 //                   expert rows), the pass-B tile of batch b - 1 and the
@@ -371,10 +371,17 @@ ln_rows_bulk(LnArgs a) {
 //                   cp.async (16 bytes a thread; completion tracked by the
 //                   stage's mbarrier, so no copy holds registers); in the
 //                   add modes they form the row values of batch b (x + res,
-//                   or combine + carry), write them to x_out and into a tile
-//                   for chain A; and they write y of batch b - 2 from its
-//                   tile and the stats chain B published;
+//                   or combine + carry) and write them to x_out (with the
+//                   un-permute also into a tile for chain A); and they write
+//                   y of batch b - 2 from its tile and the stats chain B
+//                   published;
 //   chain warp A    lane r adds row r of batch b in ascending order -> mean;
+//                   with the residual it forms x + res itself from the
+//                   staged inputs (the compute warps' operation, so the same
+//                   values; independent of the chain, they fill its issue
+//                   slots), with the un-permute it reads the compute warps'
+//                   tile (forming combine + carry there would make the
+//                   chain warp issue-bound);
 //   chain warp B    lane r accumulates (x - mean)^2 of row r of batch b - 1
 //                   as a fused multiply-add, ascending -> 1/sqrt(var/h+eps).
 //
@@ -403,7 +410,7 @@ constexpr int pipe_inputs() {
 // pass-A inputs, pass-B tile, y-pass tile and gamma / beta chunk).
 template <int MODE>
 constexpr int pipe_stages() {
-    return MODE == kLN ? 8 : (MODE == kAddLN ? 5 : 4);
+    return MODE == kLN ? 8 : (MODE == kAddLN ? 6 : 4);
 }
 
 // floats of one stage: NIN pass-A tiles, the pass-B tile, the y-pass tile,
@@ -413,17 +420,24 @@ constexpr int pipe_stage_floats() {
     return (pipe_inputs<MODE>() + 2) * kPipeTile + 2 * kPipeChunk;
 }
 
-// Dynamic shared memory: the stages, then (add modes) two tiles of row
+// Whether chain A reads the stage's pass-A inputs itself (LN, add + LN) or
+// a tile of row values the compute warps formed (the un-permute).
+template <int MODE>
+constexpr bool chain_reads_stage() {
+    return MODE != kCombineAddLN;
+}
+
+// Dynamic shared memory: the stages, then (un-permute) two tiles of row
 // values for chain A.
 template <int MODE>
 constexpr std::size_t pipe_smem() {
     return (static_cast<std::size_t>(pipe_stages<MODE>()) * pipe_stage_floats<MODE>() +
-            (MODE == kLN ? 0 : 2) * kPipeTile) * sizeof(float);
+            (chain_reads_stage<MODE>() ? 0 : 2) * kPipeTile) * sizeof(float);
 }
 
 struct PipeShared {
     std::uint64_t full[kPipeMaxStages], empty[kPipeMaxStages];
-    std::uint64_t sfull[2], sempty[2];  // compute -> chain A: row-value tiles
+    std::uint64_t sfull[2], sempty[2];  // compute -> chain A: row-value tiles (un-permute)
     std::uint64_t mfull[2], mempty[2];  // chain A -> chain B: means
     std::uint64_t ifull[2], iempty[2];  // chain B -> compute: mean and 1/std
     float mean_a[2][kPipeRows];
@@ -514,8 +528,10 @@ ln_exact_pipe(LnArgs a) {
     constexpr int CW = kPipeComputeWarps;
     constexpr int Q = kPipeChunk / 4;  // float4 of a row chunk (one per lane)
     // readers of a stage: the compute warps (y-pass tile, gamma / beta, their
-    // own pass-A copies), chain B (pass-B tile), chain A (plain LN's pass A)
-    constexpr unsigned kStageReaders = CW + (MODE == kLN ? 2u : 1u);
+    // own pass-A copies), chain B (pass-B tile), chain A (pass-A inputs,
+    // unless it reads the compute warps' row values)
+    constexpr bool kChainStage = chain_reads_stage<MODE>();
+    constexpr unsigned kStageReaders = CW + (kChainStage ? 2u : 1u);
     extern __shared__ __align__(128) float smem[];
     __shared__ PipeShared sh;
     const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -533,7 +549,7 @@ ln_exact_pipe(LnArgs a) {
     auto tile_b = [&](int st) { return stage_base(st) + NIN * kPipeTile; };
     auto tile_o = [&](int st) { return stage_base(st) + (NIN + 1) * kPipeTile; };
     auto tile_gb = [&](int st) { return stage_base(st) + (NIN + 2) * kPipeTile; };  // gamma | beta
-    float* svals = smem + S * pipe_stage_floats<MODE>();  // [2] tiles (add modes)
+    float* svals = smem + S * pipe_stage_floats<MODE>();  // [2] tiles (un-permute)
     auto row0 = [&](int j) {
         return (static_cast<std::size_t>(blockIdx.x) + static_cast<std::size_t>(j) * gridDim.x) * kPipeRows;
     };
@@ -562,35 +578,37 @@ ln_exact_pipe(LnArgs a) {
     __syncthreads();
 
     if (warp == 0) {
-        // ---- chain A: ascending sums ----
+        // ---- chain A: ascending sums of the row values of batch b ----
         float acc = 0.0f;
-        unsigned q = 0;  // pass-A ticks so far
+        unsigned q = 0;  // row-value tiles so far (un-permute)
         for (long long g = 0; g < G; ++g) {
             const int st = static_cast<int>(g % S);
             const unsigned use = static_cast<unsigned>(g / S);
             const int jb = static_cast<int>(g / NT), c = static_cast<int>(g % NT);
-            if (MODE == kLN && !warp_wait(&sh.full[st], use & 1u, abort_flag)) break;
+            if (kChainStage && !warp_wait(&sh.full[st], use & 1u, abort_flag)) break;
             if (jb < nb) {
-                const float* tile;
-                if (MODE == kLN) {
-                    tile = tile_in(st, 0);
-                } else {
+                const float* tile = tile_in(st, 0);
+                if (!kChainStage) {
                     if (!warp_wait(&sh.sfull[q & 1u], (q >> 1) & 1u, abort_flag)) break;
                     tile = svals + (q & 1u) * kPipeTile;
                 }
                 if (static_cast<int>(lane) < nrows(jb)) {
-                    const float4* row = reinterpret_cast<const float4*>(tile + lane * kPipePitch);
+                    const float4* r0 = reinterpret_cast<const float4*>(tile + lane * kPipePitch);
+                    const float4* r1 = reinterpret_cast<const float4*>(tile_in(st, NIN > 1 ? 1 : 0) + lane * kPipePitch);
 #pragma unroll 8
                     for (int i = 0; i < Q; ++i) {
-                        const float4 v = row[i];
+                        float4 v = r0[i];
+                        if (MODE == kAddLN) v = add4(v, r1[i]);  // x + res, as the compute warps form it
                         acc = __fadd_rn(acc, v.x);
                         acc = __fadd_rn(acc, v.y);
                         acc = __fadd_rn(acc, v.z);
                         acc = __fadd_rn(acc, v.w);
                     }
                 }
-                if (MODE != kLN) warp_arrive(&sh.sempty[q & 1u]);
-                ++q;
+                if (!kChainStage) {
+                    warp_arrive(&sh.sempty[q & 1u]);
+                    ++q;
+                }
                 if (c == NT - 1) {
                     const float mean = __fdiv_rn(acc, static_cast<float>(h));
                     acc = 0.0f;
@@ -599,7 +617,7 @@ ln_exact_pipe(LnArgs a) {
                     warp_arrive(&sh.mfull[jb & 1]);
                 }
             }
-            if (MODE == kLN) warp_arrive(&sh.empty[st]);
+            if (kChainStage) warp_arrive(&sh.empty[st]);
         }
     } else if (warp == 1) {
         // ---- chain B: ascending sums of squared deviations ----
@@ -731,7 +749,7 @@ ln_exact_pipe(LnArgs a) {
         float m_o[2] = {0.f, 0.f}, i_o[2] = {0.f, 0.f};
         bool ok = true;
         for (int d = 0; d < AHEAD && ok; ++d) ok = stage(d);
-        unsigned q = 0;
+        unsigned q = 0;  // row-value tiles so far (un-permute)
         for (long long g = 0; g < G && ok; ++g) {
             if (!stage(g + AHEAD)) break;
             const int st = static_cast<int>(g % S);
@@ -744,9 +762,9 @@ ln_exact_pipe(LnArgs a) {
                     std::size_t lo, hi;
                     for (int k = 0; k < 2; ++k) expert_rows(jb, k, lo, hi, ps_lok[k], ps_hok[k]);
                 }
-                if (!warp_wait(&sh.sempty[q & 1u], ((q >> 1) & 1u) ^ 1u, abort_flag)) break;
-                const int nra = nrows(jb);
+                if (!kChainStage && !warp_wait(&sh.sempty[q & 1u], ((q >> 1) & 1u) ^ 1u, abort_flag)) break;
                 float* tile = svals + (q & 1u) * kPipeTile;
+                const int nra = nrows(jb);
                 const std::size_t c4 = static_cast<std::size_t>(c) * Q + lane;
                 for (int k = 0; k < 2; ++k) {
                     const int r = cw + 8 * k;
@@ -762,10 +780,12 @@ ln_exact_pipe(LnArgs a) {
                         v = add4(combine4(lo4, hi4), v0);
                     }
                     st_l2(xo4 + (row0(jb) + r) * h4 + c4, v, keep);
-                    *reinterpret_cast<float4*>(tile + o) = v;
+                    if (!kChainStage) *reinterpret_cast<float4*>(tile + o) = v;
                 }
-                warp_arrive(&sh.sfull[q & 1u]);
-                ++q;
+                if (!kChainStage) {
+                    warp_arrive(&sh.sfull[q & 1u]);
+                    ++q;
+                }
             }
             if (jo >= 0 && jo < nb) {
                 if (c == 0) {
