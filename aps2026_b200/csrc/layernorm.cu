@@ -360,22 +360,21 @@ ln_rows_bulk(LnArgs a) {
 // chain of h dependent additions per row for each, about 17 us of FP32
 // latency per row at h = 4096. Over many rows that latency has to overlap
 // the HBM traffic, so rows go through a pipeline of persistent CTAs (two per
-// SM for plain LN and the un-permute, one for add + LN), in batches of 16
-// rows and "ticks" of one 128-float chunk of each row:
+// SM), in batches of 16 rows and "ticks" of one 128-float chunk of each row:
 //
-//   compute warps   stage, a ring of shared-memory stages ahead (4 stages
-//                   for plain LN, 6 with the residual, 2 with the
+//   compute warps   stage, a ring of shared-memory stages ahead (6 stages
+//                   for plain LN, 4 with the residual, 2 with the
 //                   un-permute, as many as fit), the pass-A inputs of batch
 //                   b (x; x and the residual; or the carry and the two
-//                   expert rows), the pass-B tile of batch b - 1 and the
-//                   y-pass tile of batch b - 2 with gamma and beta, by
-//                   cp.async (16 bytes a thread; completion tracked by the
-//                   stage's mbarrier, so no copy holds registers); in the
-//                   add modes they form the row values of batch b (x + res,
-//                   or combine + carry) and write them to x_out (with the
-//                   un-permute also into a tile for chain A); and they write
-//                   y of batch b - 2 from its tile and the stats chain B
-//                   published;
+//                   expert rows), the pass-B tile of batch b - 1 and gamma
+//                   and beta, by cp.async (16 bytes a thread; completion
+//                   tracked by the stage's mbarrier, so no copy holds
+//                   registers); in the add modes they form the row values of
+//                   batch b (x + res, or combine + carry) and write them to
+//                   x_out (with the un-permute also into a tile for chain
+//                   A); and they write y of batch b - 2 from its row values,
+//                   loaded into registers two ticks ahead, and the stats
+//                   chain B published;
 //   chain warp A    lane r adds row r of batch b in ascending order -> mean;
 //                   with the residual it forms x + res itself from the
 //                   staged inputs (the compute warps' operation, so the same
@@ -408,26 +407,26 @@ constexpr int pipe_inputs() {
 }
 
 // Stages of the ring (as many as fit in shared memory; each holds a tick's
-// pass-A inputs, pass-B tile, y-pass tile and gamma / beta chunk).
+// pass-A inputs, pass-B tile and gamma / beta chunk).
 // CTAs per SM: a tick's time is set by the chain warps, so two CTAs (twice
-// the chains, half the ring each) for plain LN and the un-permute -- 22% and
-// 5% faster than one CTA with 8 / 4 stages at 131,072 x 4096 -- and one for
-// add + LN, whose 6-stage ring beat two CTAs of 3 by 3%.
+// the chains, half the ring each). At 131,072 x 4096 that took 17% (LN),
+// 10% (add + LN) and 15% (un-permute) off one CTA with a deeper ring (8, 8
+// and 5 stages).
 template <int MODE>
 constexpr int pipe_ctas_per_sm() {
-    return MODE == kAddLN ? 1 : 2;
+    return 2;
 }
 
 template <int MODE>
 constexpr int pipe_stages() {
-    return MODE == kLN ? 4 : (MODE == kAddLN ? 6 : 2);
+    return MODE == kLN ? 6 : (MODE == kAddLN ? 4 : 2);
 }
 
-// floats of one stage: NIN pass-A tiles, the pass-B tile, the y-pass tile,
+// floats of one stage: NIN pass-A tiles, the pass-B tile,
 // and gamma | beta of the chunk
 template <int MODE>
 constexpr int pipe_stage_floats() {
-    return (pipe_inputs<MODE>() + 2) * kPipeTile + 2 * kPipeChunk;
+    return (pipe_inputs<MODE>() + 1) * kPipeTile + 2 * kPipeChunk;
 }
 
 // Whether chain A reads the stage's pass-A inputs itself (LN, add + LN) or
@@ -522,6 +521,13 @@ __device__ __forceinline__ void cp_async16_l2(void* dst, const void* src, std::u
                  "l"(policy)
                  : "memory");
 }
+__device__ __forceinline__ float4 ld_l2(const float4* p, std::uint64_t policy) {
+    float4 v;
+    asm volatile("ld.global.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(policy));
+    return v;
+}
 __device__ __forceinline__ void st_l2(float4* p, const float4& v, std::uint64_t policy) {
     asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
                  "f"(v.w), "l"(policy)
@@ -537,7 +543,7 @@ ln_exact_pipe(LnArgs a) {
     constexpr int AHEAD = S - 1;  // ticks staged ahead of the one being used
     constexpr int CW = kPipeComputeWarps;
     constexpr int Q = kPipeChunk / 4;  // float4 of a row chunk (one per lane)
-    // readers of a stage: the compute warps (y-pass tile, gamma / beta, their
+    // readers of a stage: the compute warps (gamma / beta, their
     // own pass-A copies), chain B (pass-B tile), chain A (pass-A inputs,
     // unless it reads the compute warps' row values)
     constexpr bool kChainStage = chain_reads_stage<MODE>();
@@ -557,8 +563,7 @@ ln_exact_pipe(LnArgs a) {
     auto stage_base = [&](int st) { return smem + st * pipe_stage_floats<MODE>(); };
     auto tile_in = [&](int st, int input) { return stage_base(st) + input * kPipeTile; };
     auto tile_b = [&](int st) { return stage_base(st) + NIN * kPipeTile; };
-    auto tile_o = [&](int st) { return stage_base(st) + (NIN + 1) * kPipeTile; };
-    auto tile_gb = [&](int st) { return stage_base(st) + (NIN + 2) * kPipeTile; };  // gamma | beta
+    auto tile_gb = [&](int st) { return stage_base(st) + (NIN + 1) * kPipeTile; };  // gamma | beta
     float* svals = smem + S * pipe_stage_floats<MODE>();  // [2] tiles (un-permute)
     auto row0 = [&](int j) {
         return (static_cast<std::size_t>(blockIdx.x) + static_cast<std::size_t>(j) * gridDim.x) * kPipeRows;
@@ -700,8 +705,8 @@ ln_exact_pipe(LnArgs a) {
             hok = hi < a.expert_rows;
         };
         // stages this thread's part of tick t: the pass-A inputs of batch
-        // t / NT, the pass-B tile of the batch before, the y-pass tile of the
-        // batch before that (and, warps 0 / 1, the gamma / beta chunk)
+        // t / NT, the pass-B tile of the batch before (and, warps 0 / 1, the
+        // gamma / beta chunk for the y pass of the batch before that)
         auto stage = [&](long long t) -> bool {
             if (t >= G) return true;
             const int st = static_cast<int>(t % S);
@@ -743,24 +748,29 @@ ln_exact_pipe(LnArgs a) {
                                       keep);
                 }
             }
-            if (jb >= 2 && jb - 2 < nb) {
-                const int nro = nrows(jb - 2);
-                for (int k = 0; k < 2; ++k) {
-                    const int r = cw + 8 * k;
-                    if (r < nro)  // the last read of these row values
-                        cp_async16_l2(tile_o(st) + r * kPipePitch + o_lane, sv4 + (row0(jb - 2) + r) * h4 + c4,
-                                      stream);
-                }
-                if (cw < 2) cp_async16(tile_gb(st) + cw * kPipeChunk + o_lane, (cw == 0 ? g4 : b4) + c4);
-            }
+            if (jb >= 2 && jb - 2 < nb && cw < 2)
+                cp_async16(tile_gb(st) + cw * kPipeChunk + o_lane, (cw == 0 ? g4 : b4) + c4);
             cp_async_arrive(&sh.full[st]);
             return true;
         };
         float m_o[2] = {0.f, 0.f}, i_o[2] = {0.f, 0.f};
+        // the y pass's row values (the last read of them), loaded into
+        // registers two ticks ahead: tick t's for rows cw + 8k of batch t / NT - 2
+        auto yload = [&](long long t, int k) -> float4 {
+            const int j = static_cast<int>(t / NT) - 2, cc = static_cast<int>(t % NT);
+            if (t >= G || j < 0 || j >= nb || cw + 8 * k >= nrows(j)) return zero4();
+            return ld_l2(sv4 + (row0(j) + cw + 8 * k) * h4 + static_cast<std::size_t>(cc) * Q + lane, stream);
+        };
+        float4 ya[2] = {yload(0, 0), yload(0, 1)}, yb[2] = {yload(1, 0), yload(1, 1)};
         bool ok = true;
         for (int d = 0; d < AHEAD && ok; ++d) ok = stage(d);
         unsigned q = 0;  // row-value tiles so far (un-permute)
         for (long long g = 0; g < G && ok; ++g) {
+            const float4 yc[2] = {ya[0], ya[1]};
+            ya[0] = yb[0];
+            ya[1] = yb[1];
+            yb[0] = yload(g + 2, 0);
+            yb[1] = yload(g + 2, 1);
             if (!stage(g + AHEAD)) break;
             const int st = static_cast<int>(g % S);
             const unsigned use = static_cast<unsigned>(g / S);
@@ -812,10 +822,7 @@ ln_exact_pipe(LnArgs a) {
                 const int nro = nrows(jo);
                 for (int k = 0; k < 2; ++k) {
                     const int r = cw + 8 * k;
-                    if (r < nro) {
-                        const float4 v = *reinterpret_cast<const float4*>(tile_o(st) + r * kPipePitch + o_lane);
-                        st_l2(y4 + (row0(jo) + r) * h4 + c4, ln_out4(v, m_o[k], i_o[k], gw, bw), stream);
-                    }
+                    if (r < nro) st_l2(y4 + (row0(jo) + r) * h4 + c4, ln_out4(yc[k], m_o[k], i_o[k], gw, bw), stream);
                 }
             }
             warp_arrive(&sh.empty[st]);
