@@ -925,8 +925,11 @@ int launch_smem(const LnArgs& a, cudaStream_t s) {
 // Picks, in reference order over enough rows (h a multiple of 128, aligned),
 // the chain pipeline; otherwise the register-resident variant whose
 // THREADS * V covers h / 4, else bulk-copy staging (aligned rows,
-// h % 4 == 0), else the scalar shared-memory one.
-constexpr int kPipeMinBatchesPerSm = 4;
+// h % 4 == 0), else the scalar shared-memory one. From one 16-row batch per
+// SM the pipeline beats the per-row kernels (at 6,144 and 8,192 rows by
+// 15% / 24% with the residual, 8% / 19% with the un-permute; they tie at
+// 2,048).
+constexpr int kPipeMinBatchesPerSm = 1;
 template <int MODE>
 int dispatch(const LnArgs& a, bool exact, bool vec_ok, cudaStream_t s, const char* what) {
     if (a.h * sizeof(float) > kMaxSmemRow && exact)
@@ -938,7 +941,7 @@ int dispatch(const LnArgs& a, bool exact, bool vec_ok, cudaStream_t s, const cha
     if (vec_ok && exact && a.h % kPipeChunk == 0 &&
         a.h >= static_cast<std::size_t>(MODE == kLN ? 1 : pipe_stages<MODE>()) * kPipeChunk &&
         a.rows >= static_cast<std::size_t>(kPipeMinBatchesPerSm) * kPipeRows * sm_count()) {
-        rc = launch_exact_pipe<MODE>(a, s);  // enough 16-row batches for the pipeline to fill
+        rc = launch_exact_pipe<MODE>(a, s);  // a 16-row batch or more per SM
     } else if (vec_ok && !exact && h4 <= 256 * 8) {
         if (h4 <= 256) rc = launch_reg<MODE, 256, 1, false>(a, s);
         else if (h4 <= 512) rc = launch_reg<MODE, 256, 2, false>(a, s);

@@ -436,7 +436,13 @@ def run_ours(args):
             "hbm_gbs_algorithmic": round(bpr["total"] * rows * world / (ms_per_step / 1e3) / 1e9, 1),
             "roofline": {"kernel": dominant, "bound": "hbm", "achieved": d["gbs"], "peak": peak,
                          "unit": "GB/s", "frac": round(d["gbs"] / peak, 3) if d["gbs"] else None,
-                         "peak_kind": peak_kind, "traffic": traffic},
+                         "peak_kind": peak_kind, "traffic": traffic,
+                         **({"note": "chunks run concurrently on each GPU, so the kernel's events also span the "
+                                     "other chunks' kernels sharing it: a lower bound on the kernel's own rate "
+                                     "(its one-GPU line has one chunk); step_frac is the whole step's algorithmic "
+                                     "bytes per GPU over the same peak",
+                             "step_frac": round(bpr["total"] * rows / (ms_per_step / 1e3) / 1e9 / peak, 3)}
+                            if runner.streams else {})},
             "kernels": kern,
             "kernels_note": "per launch kind: one fully instrumented step after the timed region; the dominant "
                             "kind (roofline) from events in the timed region" +

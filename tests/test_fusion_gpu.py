@@ -11,7 +11,7 @@ reference's 8x8 tile keeps each rotation pair in one thread). Compared:
     b2_layer_norm's output, in reference order (bit for bit) and in tree
     order (the statistics of the two calls may differ in the last ulp:
     tolerance);
-  - the prologue alone at 9,473 x 4,096 (the size at which b2_layer_norm takes
+  - the prologue alone at 9,473 x 4,096 (a size at which b2_layer_norm takes
     its chain pipeline) vs b2_layer_norm, bit for bit, and the statistics vs
     the CPU oracle's LayerNorm.
 """
@@ -121,7 +121,7 @@ def test_layer_norm_prologue_at_pipeline_size(harness, ops, cuda):
     import torch
 
     g = rng(63)
-    M, K = 9473, 4096  # b2_layer_norm (reference order) takes its chain pipeline here
+    M, K = 9473, 4096  # b2_layer_norm (reference order) runs its chain pipeline at this size
     xh = normal(g, (M, K))
     wh, bh = normal(g, K, 1.0, 0.1), normal(g, K, 0.0, 0.1)
     x, gamma, beta = to_dev(xh, cuda), to_dev(wh, cuda), to_dev(bh, cuda)

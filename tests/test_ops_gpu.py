@@ -70,12 +70,13 @@ def test_gather_rows_empty_and_bad_index(ops, cuda, h):
 
 # register rows (h <= 8192 tree order, <= 4096 exact order), bulk-copy staged
 # rows (aligned, h % 4 == 0, longer), scalar staged rows (h % 4 != 0); in
-# exact order, >= 4 16-row batches per SM (9,472 rows on 148 SMs) with h a
+# exact order, >= one 16-row batch per SM (2,368 rows on 148 SMs) with h a
 # multiple of 128 (and, with a residual, at least as many chunks as ring
-# stages) take the chain pipeline: a 1-row last batch (9473), h at the add
-# modes' minimum (640), an odd chunk count (1152), and many batches per CTA
-# (20000)
-PIPE_SHAPES = [(9473, 4096), (9500, 640), (9488, 1152), (20000, 1024)]
+# stages) take the chain pipeline: just above the threshold with a 1-row last
+# batch (2369), one row below it (2367, per-row kernels), a 1-row last batch
+# over several batches per CTA (9473), h at the add modes' minimum (640), an
+# odd chunk count (1152), and many batches per CTA (20000)
+PIPE_SHAPES = [(2369, 4096), (2367, 4096), (9473, 4096), (9500, 640), (9488, 1152), (20000, 1024)]
 LN_SHAPES = [(512, 4096), (7, 4096), (3, 100), (5, 4100), (2, 12288), (1, 8192), (4, 2048), (3, 16384),
              (2, 37), (4800, 4096), (5003, 4100)] + PIPE_SHAPES
 

@@ -60,8 +60,8 @@ def test_ref_gather(ops, cuda):
     oracle.assert_bitexact(to_host(out), to_host(ref_out), "b2 vs ref gather")
 
 
-# 9473 x 4096: the exact-order chain pipeline (>= 9,472 rows), 1-row last batch
-@pytest.mark.parametrize("rows,h", [(512, 4096), (9, 100), (3, 4100), (9473, 4096)])
+# 2369 and 9473 x 4096: the exact-order chain pipeline (>= 2,368 rows), 1-row last batch
+@pytest.mark.parametrize("rows,h", [(512, 4096), (9, 100), (3, 4100), (2369, 4096), (9473, 4096)])
 def test_ref_layer_norm(ops, cuda, rows, h):
     import torch
 
