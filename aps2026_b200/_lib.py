@@ -19,6 +19,7 @@ B2_ERR_CUDA = 2
 B2_ERR_DEVICE_CHECK = 3
 B2_ERR_TIMEOUT = 4
 B2_ERR_UNSUPPORTED = 5
+B2_ERR_IO = 6
 B2_FLAG_EXACT_ORDER = 1
 
 B2_CHECK_GATHER = 1
@@ -55,6 +56,8 @@ SIGNATURES: dict[str, tuple] = {
     "b2_moe_combine": (C.c_int, [_vp, _sz, _vp, _vp, _vp, _sz, _sz, _vp]),
     "b2_add": (C.c_int, [_vp, _vp, _sz, _vp]),
     "b2_prefix_trie_build": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "b2_read_inputs": (C.c_int, [C.c_char_p, _sz, _vp, _vp, _vp, _vp, _sz, _vp, _sz]),
+    "b2_write_outputs": (C.c_int, [C.c_char_p, _vp, _sz, _sz, C.c_int, _vp]),
     "b2_selfcheck_exp": (C.c_int, [_u32, _u32, _vp, _vp, _vp]),
     "b2_selfcheck_wait": (C.c_int, [C.c_uint64]),
     # struct arguments (b2_prefill_shape / _layer / _work) are passed by address

@@ -38,6 +38,11 @@ class CudaError(RuntimeError):
     """The reference's std::runtime_error from check_cuda."""
 
 
+class FileError(RuntimeError):
+    """The reference's std::runtime_error from the harness's file reader and
+    writer (src/main.cpp:144-192)."""
+
+
 def _check(rc: int, what: str) -> None:
     if rc == _lib.B2_OK:
         return
@@ -46,6 +51,8 @@ def _check(rc: int, what: str) -> None:
         raise InvalidArgument(msg)
     if rc == _lib.B2_ERR_UNSUPPORTED:
         raise InvalidArgument(f"unsupported: {msg}")
+    if rc == _lib.B2_ERR_IO:
+        raise FileError(msg)
     raise CudaError(msg)
 
 
@@ -438,3 +445,64 @@ def prefix_trie_device(ids: torch.Tensor, offsets: torch.Tensor, vocab: int = 32
                                             ws.buf.data_ptr(), ws.bytes, _stream()), "prefix_trie_device")
     n = int(count[0].item())
     return DeviceTrie(token_node[:total], node_token[:n], node_depth[:n], node_prompt[:n], n)
+
+
+# ---- input and output files of the prefill harness --------------------------------------------
+
+
+@dataclass
+class InputBatch:
+    """The prompts of an inputs.bin file in file order, packed back to back
+    as b2_prefix_trie_build takes them."""
+    ids: "object"       # numpy int32 [total tokens]
+    seq_lens: "object"  # numpy uint32 [batch]
+    max_seq_len: int    # the file's header field
+
+    def prompts(self) -> list[list[int]]:
+        import numpy as np
+
+        ends = np.cumsum(self.seq_lens, dtype=np.int64)
+        return [self.ids[e - n:e].tolist() for n, e in zip(self.seq_lens.tolist(), ends.tolist())]
+
+
+def read_inputs(path, max_len: int = 4096) -> InputBatch:
+    """Reads a variable-length prompt file as read_inputs does
+    (src/main.cpp:144-181): same checks, same messages (FileError)."""
+    import numpy as np
+
+    b, m, total = C.c_uint32(0), C.c_uint32(0), C.c_size_t(0)
+    raw = str(path).encode()
+    L = _lib.lib()
+    _check(L.b2_read_inputs(raw, max_len, C.addressof(b), C.addressof(m), C.addressof(total),
+                            None, 0, None, 0), "read_inputs")
+    lens = np.empty(b.value, np.uint32)
+    ids = np.empty(max(total.value, 1), np.int32)
+    _check(L.b2_read_inputs(raw, max_len, None, None, None, lens.ctypes.data, lens.size, ids.ctypes.data,
+                            ids.size), "read_inputs")
+    return InputBatch(ids[: total.value], lens, m.value)
+
+
+def write_outputs(path, logits) -> None:
+    """Writes [batch, vocab] fp32 logits as write_outputs does
+    (src/main.cpp:183-192), byte for byte. A CUDA tensor is streamed from the
+    device on the current stream (after the work already on it); a CPU tensor
+    or numpy array is written directly."""
+    import numpy as np
+
+    if isinstance(logits, torch.Tensor):
+        if logits.dtype != torch.float32 or logits.dim() != 2 or not logits.is_contiguous():
+            raise InvalidArgument("logits must be a contiguous 2-D float32 tensor")
+        on_dev = logits.is_cuda
+        batch, vocab = logits.shape
+        ptr = logits.data_ptr() if logits.numel() else None
+        keep = logits
+    else:
+        keep = np.ascontiguousarray(logits, dtype=np.float32)
+        if keep.ndim != 2:
+            raise InvalidArgument("logits must be 2-D")
+        on_dev = False
+        batch, vocab = keep.shape
+        ptr = keep.ctypes.data if keep.size else None
+    _check(_lib.lib().b2_write_outputs(str(path).encode(), ptr, batch, vocab, int(on_dev),
+                                       _stream() if on_dev else None), "write_outputs")
+    del keep

@@ -22,8 +22,10 @@
  *   - errors are status codes instead of the reference's exceptions:
  *     B2_ERR_INVALID_ARGUMENT where the reference throws
  *     std::invalid_argument, B2_ERR_CUDA where its check_cuda throws
- *     std::runtime_error (src/tensor.cu:370-374). b2_last_error() returns the
- *     message of the calling thread's last failure.
+ *     std::runtime_error (src/tensor.cu:370-374), B2_ERR_IO where the
+ *     harness's file reader / writer throws (src/main.cpp:144-192).
+ *     b2_last_error() returns the message of the calling thread's last
+ *     failure.
  *
  * Floating point: by default reductions (LayerNorm moments, softmax
  * denominators) are tree-shaped, the softmax and SiLU exponentials
@@ -56,7 +58,8 @@ enum b2_status {
     B2_ERR_CUDA = 2,             /* kernel launch or CUDA runtime failure     */
     B2_ERR_DEVICE_CHECK = 3,     /* an in-kernel bounds check saw a bad index */
     B2_ERR_TIMEOUT = 4,          /* a bounded device wait gave up             */
-    B2_ERR_UNSUPPORTED = 5       /* valid request outside what is built       */
+    B2_ERR_UNSUPPORTED = 5,      /* valid request outside what is built       */
+    B2_ERR_IO = 6                /* a file could not be opened, read, written */
 };
 
 /* Flags for the floating-point reductions. */
@@ -403,6 +406,54 @@ int b2_prefix_trie_device(const int32_t* ids, const uint32_t* offsets,
                           uint32_t* node_prompt, uint32_t* node_count,
                           void* workspace, size_t workspace_bytes,
                           b2_stream_t stream);
+
+/* ---- input and output files of the prefill harness ----------------------------- */
+
+/*
+ * HOST function, replaces read_inputs (src/main.cpp:144-181). Reads the
+ * variable-length prompt file:
+ *   uint32 batch, uint32 max_seq_len, then `batch` times
+ *   uint32 len, int32 ids[len]                      (little-endian)
+ * and returns the prompts packed back to back in file order -- the `ids` /
+ * `seq_lens` pair that b2_prefix_trie_build takes (b2_prefix_trie_device
+ * takes ids and the running sum of seq_lens as offsets).
+ * Call it with seq_lens = ids = NULL to learn the sizes (*batch_out,
+ * *max_seq_out, *total_out = sum of the lengths; any of the three may be
+ * NULL), then with buffers of at least batch and total entries. Token ids
+ * are returned as stored (b2_prefix_trie_build checks the vocabulary, as
+ * src/model.cu:55-58 does). max_len is the largest accepted max_seq_len
+ * (MAX_POSITION_EMBEDDINGS = 4096 in include/config.h:16). The whole file is
+ * validated on every call. Errors, in the reference's order and with its
+ * messages (b2_last_error): B2_ERR_IO "cannot open input: <path>", "invalid
+ * input header" (shorter than 8 bytes, batch or max_seq_len 0, max_seq_len
+ * above max_len), "invalid sequence length in input" (a length field cut
+ * short, 0, or above max_seq_len), "truncated input" (fewer ids than the
+ * length says); bytes after the last prompt are ignored, as there.
+ * B2_ERR_INVALID_ARGUMENT: null path, only one of seq_lens / ids given, or
+ * a buffer below the sizes.
+ */
+int b2_read_inputs(const char* path, size_t max_len, uint32_t* batch_out,
+                   uint32_t* max_seq_out, size_t* total_out, uint32_t* seq_lens,
+                   size_t seq_lens_cap, int32_t* ids, size_t ids_cap);
+
+/*
+ * HOST function, replaces write_outputs (src/main.cpp:183-192). Writes the
+ * prefill output file byte for byte as the reference does:
+ *   uint32 batch, uint32 vocab, float logits[batch][vocab]  (little-endian)
+ * logits is row-major [batch, vocab] fp32, in device memory when
+ * logits_on_device != 0 (streamed through two 4 MiB pinned staging buffers
+ * by copies on `stream`, one chunk written while the next copies; the call
+ * orders itself after the work already on `stream`), else host memory
+ * (written directly; no CUDA call is made). Synchronous: returns once the
+ * file is closed. The pinned buffers are allocated and freed per call (a
+ * file write, not a hot-path step). Errors: B2_ERR_IO "cannot open output:
+ * <path>" / "failed while writing output: <path>" (the reference's
+ * messages); B2_ERR_INVALID_ARGUMENT for a null path, null logits with
+ * batch * vocab > 0, or batch / vocab above UINT32_MAX (the reference would
+ * truncate them to 32 bits); B2_ERR_CUDA for a failed copy.
+ */
+int b2_write_outputs(const char* path, const float* logits, size_t batch,
+                     size_t vocab, int logits_on_device, b2_stream_t stream);
 
 /* ---- diagnostics --------------------------------------------------------------- */
 

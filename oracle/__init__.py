@@ -7,6 +7,11 @@ reference-built checker library.
 - ``_ref/libref.so`` (oracle/ref_harness.cu): the reference's own
   src/tensor.cu compiled from where it lies; its kernels run on a GPU, its
   host ops anywhere.
+- ``_ref/libio_ref.so`` (oracle/io_harness.cu): the reference harness's own
+  prompt-file reader and output-file writer (src/main.cpp:144-192); host
+  only.
+- ``outputs_bytes`` / ``parse_inputs`` below: numpy restatements of those two
+  file formats.
 
 Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline /
 reference arm may use this package. The aps2026_b200 package never imports it.
@@ -22,6 +27,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libref.so"
+IO_REF_SO = HERE / "_ref" / "libio_ref.so"
 
 _vp, _sz, _f32, _i = C.c_void_p, C.c_size_t, C.c_float, C.c_int
 
@@ -103,6 +109,72 @@ def ref() -> C.CDLL:
             fn.restype, fn.argtypes = _i, args
         _ref = h
     return _ref
+
+
+_io_ref = None
+
+
+def io_ref_available() -> bool:
+    return IO_REF_SO.exists()
+
+
+def io_ref() -> C.CDLL:
+    """The reference's own read_inputs / write_outputs (src/main.cpp:144-192)
+    behind io_harness.cu; raises if it was never built."""
+    global _io_ref
+    if _io_ref is None:
+        if not IO_REF_SO.exists():
+            raise FileNotFoundError(f"{IO_REF_SO} not built (needs the reference tree)")
+        h = C.CDLL(str(IO_REF_SO))
+        h.io_ref_error.restype, h.io_ref_error.argtypes = C.c_char_p, []
+        h.io_ref_write_outputs.restype = _i
+        h.io_ref_write_outputs.argtypes = [C.c_char_p, _vp, _sz, _sz]
+        h.io_ref_read_inputs.restype = _i
+        h.io_ref_read_inputs.argtypes = [C.c_char_p, _vp, _vp, _vp, _vp, _sz, _vp, _sz]
+        _io_ref = h
+    return _io_ref
+
+
+def outputs_bytes(logits) -> bytes:
+    """The output file write_outputs (src/main.cpp:183-192) makes of a
+    [batch, vocab] fp32 matrix: uint32 batch, uint32 vocab, the floats
+    row-major, all little-endian."""
+    a = np.ascontiguousarray(logits, dtype="<f4")
+    return np.array(a.shape, dtype="<u4").tobytes() + a.tobytes()
+
+
+def inputs_bytes(prompts, max_seq_len=None) -> bytes:
+    """The prompt file read_inputs (src/main.cpp:144-181) reads: uint32 batch,
+    uint32 max_seq_len, then per prompt uint32 length and int32 ids."""
+    m = max(len(p) for p in prompts) if max_seq_len is None else max_seq_len
+    out = [np.array([len(prompts), m], dtype="<u4").tobytes()]
+    for p in prompts:
+        out.append(np.array([len(p)], dtype="<u4").tobytes() + np.asarray(p, dtype="<i4").tobytes())
+    return b"".join(out)
+
+
+def parse_inputs(data: bytes, max_len: int = 4096):
+    """read_inputs (src/main.cpp:152-181) restated over the file's bytes:
+    returns (prompts as lists, max_seq_len), or raises RuntimeError with the
+    reference's message, its checks taken in its order."""
+    if len(data) < 8:
+        raise RuntimeError("invalid input header")
+    batch, max_seq = np.frombuffer(data[:8], dtype="<u4").tolist()
+    if batch == 0 or max_seq == 0 or max_seq > max_len:
+        raise RuntimeError("invalid input header")
+    pos, prompts = 8, []
+    for _ in range(batch):
+        if len(data) - pos < 4:
+            raise RuntimeError("invalid sequence length in input")
+        n = int(np.frombuffer(data[pos:pos + 4], dtype="<u4")[0])
+        pos += 4
+        if n == 0 or n > max_seq:
+            raise RuntimeError("invalid sequence length in input")
+        if len(data) - pos < 4 * n:
+            raise RuntimeError("truncated input")
+        prompts.append(np.frombuffer(data[pos:pos + 4 * n], dtype="<i4").tolist())
+        pos += 4 * n
+    return prompts, max_seq
 
 
 def f32(a) -> np.ndarray:
