@@ -275,8 +275,11 @@ attention_tree_kernel(AttnArgs a) {
 //                  lo rows of the 32 keys (K-major, 128-byte swizzle), and a
 //                  ring of 2 value tiles hi / lo [32 keys x 128 dims] (the B
 //                  operand of P V with N = dims contiguous: MN-major,
-//                  128-byte rows with 32-byte swizzle granules); O [128 dims
-//                  / 4][128 MMA rows] float4s.
+//                  128-byte rows with 32-byte swizzle granules);
+//   registers      O, 64 floats per softmax thread (its half of a row's 128
+//                  dims; 128 registers a thread is the cap for 13 warps, as
+//                  the SM's four register-file quarters hold 4, 3, 3 and 3
+//                  of them).
 // Warp roles: 8-9 stage key tiles, 10-11 value tiles (16-byte cp.async
 // copies of the planes into the swizzled layouts); 12 issues the MMAs --
 // S(t + 1) as soon as S(t) has been read, P V(t) once P(t) is written; 0-7
@@ -289,7 +292,8 @@ attention_tree_kernel(AttnArgs a) {
 // p = 2^(s2 - m), 0 outside the row's window), and the previous tile's P V
 // is folded into O as O = O * 2^(m_old - m) + PV in FP32 round-to-nearest
 // (the tensor core's accumulator truncates; chaining every tile there biased
-// long windows by ~1e-6). The epilogue writes O * (1 / l): the softmax of
+// long windows by ~1e-6), after P(t) is stored and before P V(t) may
+// overwrite the P V columns. The epilogue writes O * (1 / l): the softmax of
 // the tree-order SIMT kernel, formed in another order. Blocks that are not a
 // path (prompt boundaries, shared-prefix branch points) are listed for
 // attention_tree_block.
@@ -304,9 +308,9 @@ constexpr std::uint32_t kColQh = 0, kColQl = 128, kColO = 256, kColS = 384, kCol
 constexpr std::uint32_t kTcCols = 512;
 constexpr int kTcTileBytes = 16 * 1024;  // one operand plane of a tile: 32 x 128 fp32
 constexpr int kTcStageBytes = 2 * kTcTileBytes;  // hi, lo
-// rings + O + 1024-byte alignment (193 KB: one CTA per SM, each allocating
-// all 512 tensor-memory columns)
-constexpr std::size_t kTcSmem = (kTcKStages + kTcVStages) * kTcStageBytes + 128 * 128 * 4 + 1024;
+// rings + 1024-byte alignment (129 KB; one CTA per SM, by its registers, and
+// each allocates all 512 tensor-memory columns)
+constexpr std::size_t kTcSmem = (kTcKStages + kTcVStages) * kTcStageBytes + 1024;
 
 // Byte offset of dims 4c .. 4c + 3 of key j's hi row in a key stage: per
 // 32-dim block (8192 bytes) the 32 hi rows then the 32 lo rows (the lo row
@@ -457,10 +461,9 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
     __shared__ volatile int abort_s;
     __shared__ std::size_t pos0_s;
     __shared__ const std::uint32_t* chain_s;
-    // 1024-byte aligned stages (swizzle atoms): keys, values, then O
+    // 1024-byte aligned stages (swizzle atoms): keys, then values
     unsigned char* kring = tc_raw + ((1024 - (smem_addr(tc_raw) & 1023u)) & 1023u);
     unsigned char* vring = kring + kTcKStages * kTcStageBytes;
-    float4* oacc = reinterpret_cast<float4*>(vring + kTcVStages * kTcStageBytes);
 
     const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const std::size_t kh = blockIdx.x % a.kv_heads;
@@ -613,23 +616,18 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
             tc::st_wait();
             tc::fence_before_sync();
             mbar_arrive(&qfull);
-            for (int c = 0; c < 16; ++c) oacc[(16 * h + c) * 128 + m] = zero4();
         }
+        float oreg[64];  // this half of the row's O: dims 64h .. 64h + 63
+#pragma unroll
+        for (int c = 0; c < 64; ++c) oreg[c] = 0.0f;
         // folds this half of the P V of the tile issued last into O: O = O * alpha + PV
         auto fold = [&](float alpha) {
-            for (int c0 = 0; c0 < 64; c0 += 32) {
-                float o[32];
-                tc::ld32(tmem + lane_base + kColO + 64 * h + c0, o);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    float4* dst = oacc + (16 * h + (c0 >> 2) + q) * 128 + m;
-                    float4 x = *dst;
-                    x.x = __fmaf_rn(x.x, alpha, o[4 * q]);
-                    x.y = __fmaf_rn(x.y, alpha, o[4 * q + 1]);
-                    x.z = __fmaf_rn(x.z, alpha, o[4 * q + 2]);
-                    x.w = __fmaf_rn(x.w, alpha, o[4 * q + 3]);
-                    *dst = x;
-                }
+            for (int c0 = 0; c0 < 64; c0 += 16) {
+                float o[16];
+                tc::ld16(tmem + lane_base + kColO + 64 * h + c0, o);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) oreg[c0 + j] = __fmaf_rn(oreg[c0 + j], alpha, o[j]);
             }
         };
         const float scale2 = __fmul_rn(a.scale, 1.4426950408889634f);  // scale * log2(e)
@@ -683,19 +681,17 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
             }
             l = __fmaf_rn(l, alpha, __fadd_rn(l0, l1));
             mx = mn;
-            if (t > 0) {  // P V(t - 1) done: fold it, and P's columns are free
+            if (t > 0) {  // P V(t - 1) done: P's columns are free, and it can be folded
                 ok = __all_sync(0xffffffffu, tc_wait(&ofull, (t - 1) & 1, &abort_s));
-                if (ok) {
-                    tc::fence_after_sync();
-                    fold(alpha_prev);
-                }
+                if (ok) tc::fence_after_sync();
             }
-            alpha_prev = alpha;
             if (ok) {
                 tc::st16(tmem + lane_base + kColPh + 16 * h, p);
                 tc::st16(tmem + lane_base + kColPl + 16 * h, pl);
+                if (t > 0) fold(alpha_prev);  // (P V's columns are read before pfull lets P V(t) overwrite them)
                 tc::st_wait();
             }
+            alpha_prev = alpha;
             tc::fence_before_sync();
             mbar_arrive(&pfull);  // also: this thread's reads of the P V columns are done
         }
@@ -712,11 +708,10 @@ attention_tree_tc(AttnArgs a, const float* split, std::uint32_t* rest_count, std
             const float inv = __fdiv_rn(1.0f, __fadd_rn(sum_x[0][m], sum_x[1][m]));
             float4* orow =
                 reinterpret_cast<float4*>(a.out + ((n0 + ri) * a.q_heads + kh * kGroup + hg) * 128 + 64 * h);
-            for (int c = 0; c < 16; ++c) {
-                const float4 x = oacc[(16 * h + c) * 128 + m];
-                st_plain(orow + c, make_float4(__fmul_rn(x.x, inv), __fmul_rn(x.y, inv), __fmul_rn(x.z, inv),
-                                               __fmul_rn(x.w, inv)));
-            }
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+                st_plain(orow + c, make_float4(__fmul_rn(oreg[4 * c], inv), __fmul_rn(oreg[4 * c + 1], inv),
+                                               __fmul_rn(oreg[4 * c + 2], inv), __fmul_rn(oreg[4 * c + 3], inv)));
         }
     }
     tc::fence_before_sync();
